@@ -1,0 +1,466 @@
+#!/usr/bin/env python
+"""Benchmark of LMPool's KV move path on B200 (one JSON line on rank 0).
+
+Metric: "KV move GB/s per pair (gather->NVLink->scatter,
+device-timed) vs blocks moved"; GB = 1e9 bytes of KV payload
+P = B * L * 2 * block_size * kv_heads * head_dim * 2 bytes moved per step
+(ModelRunner.kv_transfer_bytes, model_runner.py:808-820).
+
+Workloads (synthetic bf16 N(0,1) caches, seeded randperm block ids):
+  --gpus 1   BASELINE config 2: one GPU, Qwen3-0.6B KV geometry (L=28, H=8,
+             D=128, block_size=256), 2048-block cache (60 GB); a step moves
+             B=512 fragmented blocks inside the cache (gather+scatter in one
+             launch). The B sweep {1,4,16,64,256,512} is reported in "sweep".
+  --gpus N>1 BASELINE config 4 phase A: ranks (0,1), (2,3), ... move
+             B=128 blocks each way at once at Qwen3-8B geometry (L=36,
+             1536-block cache per rank, 58 GB); a step is one exchange
+             (publish -> wait_armed -> push over NVLink -> wait_done).
+  --impl reference  the reference algorithm on the host cores (C oracle:
+             pack into a payload, then unpack; rank 0 only), same geometry.
+
+Timing: W untimed warm-up steps, then K steps between a barrier and a
+device synchronisation, CUDA events on the launching stream, max over ranks.
+Every step's inputs exceed the 126 MB L2 (config 2: 15 GB read + 15 GB
+written per step; config 4: 4.8 GB per direction), so no flush is needed for
+the headline; the sweep flushes L2 before each timed launch.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "KV move GB/s per pair (gather→NVLink→scatter, device-timed) vs blocks moved"
+LOCAL = dict(workload="config2: 1-GPU local gather+scatter, Qwen3-0.6B KV geometry", L=28, N=2048, bs=256, H=8,
+             D=128, B=512)
+PAIRS = dict(workload="config4 phase A: disjoint NVLink pairs, both directions at once, Qwen3-8B KV geometry", L=36,
+             N=1536, bs=256, H=8, D=128, B=128)
+SWEEP_B = [1, 4, 16, 64, 256, 512]
+NVLINK_PEER_GBS = 770.0     # measured peer copy per direction on this pool (profiling recipe)
+FALLBACK_HBM_GBS = 6650.0
+CPU_SAMPLE_BLOCKS = 16
+L2_FLUSH_BYTES = 512 << 20
+
+
+def payload_bytes(g: dict, blocks: int) -> int:
+    return blocks * g["L"] * 2 * g["bs"] * g["H"] * g["D"] * 2
+
+
+def hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback (profiling recipe, 6.65 TB/s)"
+
+
+def profile_traffic(name: str) -> float | None:
+    """dram bytes per launch recorded in a committed ncu summary (profiles/<name>.txt)."""
+    p = ROOT / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    m = re.search(r"^dram_bytes_per_launch_full_size:\s*([0-9.eE+]+)", p.read_text(), re.M)
+    return float(m.group(1)) if m else None
+
+
+def seeded_perm(n: int, seed: int) -> list[int]:
+    g = torch.Generator().manual_seed(int(seed))
+    return torch.randperm(int(n), generator=g).tolist()
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of one GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.out, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.flush()
+        self.out.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.out.read())) if len(r) >= 9]
+        os.unlink(self.out.name)
+        sm, smax, power = [], [], []
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                power.append(float(r[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+def merge_clocks(items: list[dict]) -> dict:
+    sms = [c["sm_mhz"] for c in items if c.get("sm_mhz")]
+    out = {"sm_mhz": statistics.median(sms) if sms else None,
+           "sm_max_mhz": max((c["sm_max_mhz"] for c in items if c.get("sm_max_mhz")), default=None),
+           "reasons": sorted({r for c in items for r in c.get("reasons", [])}),
+           "samples": sum(c.get("samples", 0) for c in items)}
+    return out
+
+
+def cpu_reference(g: dict, blocks: int, steps: int, warmup: int, min_seconds: float = 0.0) -> dict:
+    """The reference algorithm (pack into a payload, then unpack; kv_transfer.py:229-276)
+    on the host cores through the C oracle, on a bounded sample of the workload."""
+    from oracle import c_oracle
+
+    threads = c_oracle.default_threads()
+    torch.set_num_threads(threads)
+    n = 2 * blocks + 64
+    shape = (2, g["L"], n, g["bs"], g["H"], g["D"])
+    cache = torch.zeros(shape, dtype=torch.bfloat16)
+    perm = seeded_perm(n, 0)
+    src, dst = perm[:blocks], perm[blocks:2 * blocks]
+    payload = torch.empty((g["L"], 2, blocks, g["bs"], g["H"], g["D"]), dtype=torch.bfloat16)
+    cache.fill_(1.0)
+    for _ in range(max(1, warmup)):
+        c_oracle.swap_planned(cache, src, cache, dst, nthreads=threads, payload=payload)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < steps or (time.perf_counter() - t_start) < min_seconds:
+        t0 = time.perf_counter()
+        c_oracle.swap_planned(cache, src, cache, dst, nthreads=threads, payload=payload)
+        times.append(time.perf_counter() - t0)
+    p = payload_bytes(g, blocks)
+    mean = sum(times) / len(times)
+    return {"value": p / mean / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{blocks} blocks ({p / 2**20:.0f} MiB payload) of the same geometry, cache of {n} blocks, "
+                      f"{len(times)} timed pack+unpack passes ({sum(times):.1f} s), C oracle, {threads} threads",
+            "ms_per_step": mean * 1e3, "steps": len(times)}
+
+
+# ---------------------------------------------------------------------------
+# 1 GPU: config 2
+# ---------------------------------------------------------------------------
+
+def bench_local(args) -> dict:
+    from lmpool_b200 import _capi
+    from lmpool_b200 import kv_transfer as kt
+    from lmpool_b200.layout import affine_layout
+
+    g = LOCAL
+    dev_idx = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(dev_idx)
+    dev = torch.device("cuda", dev_idx)
+    shape = (2, g["L"], g["N"], g["bs"], g["H"], g["D"])
+    cache = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    cache.normal_(generator=torch.Generator(device=dev).manual_seed(0))
+    lay = affine_layout(cache, g["L"])
+    perm = seeded_perm(g["N"], 0)
+    stream = torch.cuda.current_stream(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def ids_for(b):
+        return (torch.tensor(perm[:b], dtype=torch.int64, device=dev),
+                torch.tensor(perm[b:2 * b], dtype=torch.int64, device=dev))
+
+    B = g["B"]
+    src_t, dst_t = ids_for(B)
+    P = payload_bytes(g, B)
+
+    def step():
+        kt._launch_move(dev_idx, lay, lay, src_t, dst_t, B, status, stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev_idx).start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end) / args.steps
+    if int(status.item()) != 0:
+        raise RuntimeError(f"kernel status {status.item()}")
+    # correctness spot check of the timed workload
+    for i in (0, B // 2, B - 1):
+        if not torch.equal(cache[:, :, perm[B + i]].view(torch.int16), cache[:, :, perm[i]].view(torch.int16)):
+            raise RuntimeError("moved block differs from its source")
+
+    value = P / (ms * 1e-3) / 1e9
+    peak, peak_src = hbm_peak()
+    achieved = 2 * P / (ms * 1e-3) / 1e9
+    traffic = profile_traffic("move_local_config2")
+
+    # B sweep, L2 flushed before each timed launch
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    sweep = []
+    for b in SWEEP_B:
+        s_t, d_t = ids_for(b)
+        pb = payload_bytes(g, b)
+        for _ in range(3):
+            kt._launch_move(dev_idx, lay, lay, s_t, d_t, b, status, stream)
+        iters = 30 if b <= 64 else 10
+        times = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            kt._launch_move(dev_idx, lay, lay, s_t, d_t, b, status, stream)
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        t = statistics.median(times) * 1e-3
+        sweep.append({"blocks": b, "bytes": pb, "ms": t * 1e3, "GB/s": pb / t / 1e9,
+                      "hbm_GB/s": 2 * pb / t / 1e9, "frac_hbm": 2 * pb / t / 1e9 / peak})
+    del flush
+
+    # end to end through the public API: host id lists -> pinned -> device,
+    # one launch, device -> host status read, every step
+    e2e_steps = max(3, min(args.steps, 50))
+    for _ in range(2):
+        kt.move_blocks(cache, g["L"], perm[:B], perm[B:2 * B], synchronize=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        kt.move_blocks(cache, g["L"], perm[:B], perm[B:2 * B], synchronize=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+
+    tune = _capi.Tuning()
+    _capi.lib().kvx_get_tuning(_capi.ctypes.byref(tune))
+    del cache
+    torch.cuda.empty_cache()
+    cpu = cpu_reference(g, CPU_SAMPLE_BLOCKS, steps=3, warmup=1, min_seconds=10.0)
+    return {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: bf16 N(0,1) KV cache (device generator seed 0), block ids from randperm(2048, seed 0)",
+        "config": {"workload": g["workload"], "num_layers": g["L"], "num_blocks": g["N"], "block_size": g["bs"],
+                   "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_moved": B, "payload_bytes_per_step": P,
+                   "src_ids": "randperm[:512]", "dst_ids": "randperm[512:1024]",
+                   "l2": "inputs larger than L2 (15 GB read + 15 GB written per step); sweep flushes L2",
+                   "parallelism": "replicas only"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_source": peak_src,
+                     "algorithmic_bytes_per_launch": 2 * P, "kernel_ms": ms},
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": P / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 4,
+                "api": "lmpool_b200.kv_transfer.move_blocks(host id lists, synchronize=True)"},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "sweep": sweep,
+        "kernel": {"variant": {0: "auto", 1: "register", 2: "bulk"}[tune.variant], "launches_per_step": 1},
+    }
+
+
+# ---------------------------------------------------------------------------
+# N GPUs: config 4 phase A
+# ---------------------------------------------------------------------------
+
+def bench_pairs(args) -> dict | None:
+    import torch.distributed as dist
+
+    from lmpool_b200 import kv_transfer as kt
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    if world % 2:
+        raise SystemExit("--gpus must be even for the pair benchmark")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    g = PAIRS
+    shape = (2, g["L"], g["N"], g["bs"], g["H"], g["D"])
+    cache = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+    cache.normal_(generator=torch.Generator(device=dev).manual_seed(rank))
+    kt.register_kv_cache(cache, g["L"])
+    pairs = [(r, r + 1) for r in range(0, world, 2)]
+    kt.prewarm_p2p_pairs(pairs, num_layers=g["L"], block_size=g["bs"], num_kv_heads=g["H"], head_dim=g["D"],
+                         num_blocks=2, dtype=torch.bfloat16, timeout_s=60)
+    partner = rank + 1 if rank % 2 == 0 else rank - 1
+    B = g["B"]
+    src_ids = seeded_perm(g["N"], 1000 + rank)[:B]
+    # destination ids on this rank for the partner's blocks: distinct from
+    # this rank's own outgoing sources
+    free = [b for b in seeded_perm(g["N"], 2000 + rank) if b not in set(src_ids)]
+    dst_ids = free[:B]
+    ep = kt._ENDPOINTS[local]
+    link = ep.get_link(partner)
+    stream = torch.cuda.current_stream(dev)
+    src_t = torch.tensor(src_ids, dtype=torch.int64, device=dev)
+    dst_t = torch.tensor(dst_ids, dtype=torch.int64, device=dev)
+    P = payload_bytes(g, B)
+
+    def step():
+        token = ep.next_token(partner)
+        ep.publish(link, dst_t, B, token, stream)
+        ep.wait_armed(link, B, 60.0, stream)
+        ep.push(ep.cache, [(link, link.cache, src_t, B)], stream)
+        ep.wait_done(partner, token, 60.0, stream)
+
+    ep.status.zero_()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local).start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    bits = int(ep.status.item())
+    # correctness: checksums of what this rank sent vs what its partner holds
+    sums_src = cache[:, :, src_ids].view(torch.int16).reshape(2, g["L"], B, -1).sum(-1, dtype=torch.int64).cpu()
+    sums_dst = cache[:, :, dst_ids].view(torch.int16).reshape(2, g["L"], B, -1).sum(-1, dtype=torch.int64).cpu()
+    gathered: list = [None] * world
+    dist.all_gather_object(gathered, {"rank": rank, "src": sums_src, "dst": sums_dst, "bits": bits, "clk": clk})
+    ok = all(item["bits"] == 0 for item in gathered)
+    ok &= torch.equal(gathered[partner]["src"], sums_dst)
+
+    # end to end: host id lists through swap_batch (pinned H2D + status D2H per step)
+    e2e_steps = max(3, min(args.steps, 30))
+    for _ in range(2):
+        kt.swap_batch([(partner, src_ids)], [(partner, dst_ids)])
+    dist.barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(e2e_steps):
+        kt.swap_batch([(partner, src_ids)], [(partner, dst_ids)])
+    e3.record(stream)
+    torch.cuda.synchronize()
+    t2 = torch.tensor([e2.elapsed_time(e3) / e2e_steps], dtype=torch.float64, device=dev)
+    dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item())
+    oks = [None] * world
+    dist.all_gather_object(oks, bool(ok))
+    kt.shutdown()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    if not all(oks):
+        raise RuntimeError("pair transfer verification failed")
+    value = world * P / (ms * 1e-3) / 1e9
+    per_dir = P / (ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic: bf16 N(0,1) KV caches (device generator seed = rank), seeded randperm ids",
+        "config": {"workload": g["workload"], "num_layers": g["L"], "num_blocks": g["N"], "block_size": g["bs"],
+                   "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_moved_per_direction": B,
+                   "payload_bytes_per_rank_per_step": P, "pairs": pairs,
+                   "l2": "inputs larger than L2 (4.8 GB per direction per step)",
+                   "parallelism": f"{world // 2} NVLink pairs, push over CUDA IPC"},
+        "roofline": {"bound": "nvlink", "achieved": per_dir, "peak": NVLINK_PEER_GBS, "unit": "GB/s",
+                     "frac": per_dir / NVLINK_PEER_GBS, "traffic": None,
+                     "peak_source": "peer copy per direction measured on this pool (profiling recipe); 900 nominal"},
+        "e2e": {"value": world * P / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 4,
+                "api": "lmpool_b200.kv_transfer.swap_batch(host id lists)"},
+        "gpu_launches": 4 * args.steps,
+        "clocks": merge_clocks([item["clk"] for item in gathered]),
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--variant", choices=["auto", "register", "bulk"], default="auto")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        g = LOCAL if args.gpus <= 1 else PAIRS
+        res = cpu_reference(g, CPU_SAMPLE_BLOCKS, steps=args.steps, warmup=args.warmup)
+        line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": res["steps"], "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic bf16 KV cache, seeded randperm block ids",
+                "config": {"workload": g["workload"], "num_layers": g["L"], "block_size": g["bs"],
+                           "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_per_step": CPU_SAMPLE_BLOCKS},
+                "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    from lmpool_b200 import _capi
+
+    if args.variant != "auto":
+        t = _capi.Tuning(variant={"register": 1, "bulk": 2}[args.variant])
+        _capi.check(_capi.lib().kvx_set_tuning(_capi.ctypes.byref(t)), "kvx_set_tuning")
+    if world > 1 or args.gpus > 1:
+        res = bench_pairs(args)
+    else:
+        res = bench_local(args)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

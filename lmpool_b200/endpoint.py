@@ -1,0 +1,319 @@
+"""Per-GPU transfer endpoint: mailbox, peer mappings and the pair protocol.
+
+One :class:`TransferEndpoint` exists per (process, GPU). It owns this rank's
+mailbox (a small device region other ranks write into over NVLink), the
+mappings of peers' KV caches and mailboxes (CUDA IPC for other processes,
+plain peer pointers inside one process), and the completion tokens of every
+directed pair. It replaces the per-pair NCCL communicators of
+``prewarm_p2p_pairs`` (src/lmpool/engine/kv_transfer.py:40-119) and the
+``dist.send``/``dist.recv`` of ``swap_in`` (kv_transfer.py:463-470).
+
+Protocol of one transfer ``src -> dst`` (B blocks):
+
+=================================  ==========================================
+destination (execute_swap_in)      source (execute_swap_out)
+=================================  ==========================================
+token = next token for src
+publish: ids -> src mailbox,
+  count, arm = token               wait_armed: arm > last consumed
+                                     (bounded), count == B, go = token
+wait_done: flag == token           push: src blocks -> dst cache over NVLink;
+  (bounded)                          last CTA: flag = token (release, sys)
+stream sync, status check          stream sync, status check
+=================================  ==========================================
+
+Tokens are issued by the destination and only grow, so a late or repeated
+completion can never satisfy a newer transfer, and a source that missed a
+transfer simply consumes the newest arm. All waits are bounded and end with
+an error status, never a hang or a trap.
+"""
+from __future__ import annotations
+
+import ctypes
+import logging
+import os
+import threading
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _capi
+from .layout import CacheLayout
+
+logger = logging.getLogger(__name__)
+
+DEFAULT_TIMEOUT_S = float(os.environ.get("LMPOOL_B200_KV_TIMEOUT_S", "120"))
+MAX_TARGETS_PER_LAUNCH = 8
+
+
+def _dtype_from_name(name: str) -> torch.dtype:
+    dt = getattr(torch, str(name).split(".")[-1], None)
+    return dt if isinstance(dt, torch.dtype) else torch.uint8
+
+
+def timeout_ns(seconds: float | None) -> int:
+    s = DEFAULT_TIMEOUT_S if seconds is None else float(seconds)
+    return max(1, int(s * 1e9))
+
+
+@dataclass
+class PeerRecord:
+    """What a rank publishes about itself to the others (plain data)."""
+
+    rank: int
+    pid: int
+    hostname: str
+    device: int
+    mailbox_handle: bytes
+    mailbox_offset: int
+    mailbox_ptr: int
+    mailbox_peers: int
+    mailbox_max_blocks: int
+    cache_handle: bytes | None = None
+    cache_offset: int = 0
+    cache_ptr: int = 0
+    cache_geometry: dict | None = None
+    extra: dict = field(default_factory=dict)
+
+
+@dataclass
+class PeerLink:
+    """This process's view of one peer: its mailbox and cache, mapped here."""
+
+    peer: int
+    mailbox: _capi.Mailbox
+    cache: CacheLayout | None
+    closers: list = field(default_factory=list)  # IPC handles to release on close
+    poisoned: str | None = None
+
+
+class TransferEndpoint:
+    """Mailbox, peer links and pair tokens of one rank on one GPU."""
+
+    def __init__(self, rank: int, world_size: int, device: int, max_blocks: int):
+        if world_size <= 0 or not (0 <= rank < world_size):
+            raise RuntimeError(f"bad rank {rank} for world size {world_size}")
+        self.rank = int(rank)
+        self.world_size = int(world_size)
+        self.device = int(device)
+        self.lib = _capi.lib()
+        mb = _capi.Mailbox()
+        _capi.check(self.lib.kvx_mailbox_create(self.device, self.world_size, int(max_blocks), ctypes.byref(mb)),
+                    "kvx_mailbox_create")
+        self.mailbox = mb
+        self.cache: CacheLayout | None = None
+        self._cache_ref = None
+        self.links: dict[int, PeerLink] = {}
+        self.tokens_issued: dict[int, int] = {}
+        self._lock = threading.Lock()
+        self._ipc_maps: dict[bytes, list] = {}   # handle -> [base address, references]
+        # word 0: this endpoint's per-call status (zeroed per transfer)
+        self.status = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
+        self.closed = False
+
+    # -- local cache ---------------------------------------------------------
+    def set_cache(self, layout: CacheLayout, keepalive=None) -> None:
+        if layout.device.type != "cuda" or layout.device.index != self.device:
+            raise RuntimeError(f"cache lives on {layout.device}, endpoint is on cuda:{self.device}")
+        if layout.num_blocks > self.mailbox.max_blocks:
+            raise RuntimeError(
+                f"cache has {layout.num_blocks} blocks, mailbox holds {self.mailbox.max_blocks}: "
+                "create the endpoint with max_blocks >= num_blocks"
+            )
+        self.cache = layout
+        self._cache_ref = keepalive
+
+    # -- records and links ---------------------------------------------------
+    def export_record(self, hostname: str = "") -> PeerRecord:
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _capi.check(self.lib.kvx_ipc_export(self.device, ctypes.c_void_p(self.mailbox.base), handle, ctypes.byref(off)),
+                    "kvx_ipc_export(mailbox)")
+        rec = PeerRecord(rank=self.rank, pid=os.getpid(), hostname=hostname, device=self.device,
+                         mailbox_handle=handle.raw, mailbox_offset=off.value, mailbox_ptr=self.mailbox.base,
+                         mailbox_peers=self.mailbox.max_peers, mailbox_max_blocks=self.mailbox.max_blocks)
+        if self.cache is not None:
+            ch = ctypes.create_string_buffer(64)
+            coff = ctypes.c_uint64(0)
+            _capi.check(self.lib.kvx_ipc_export(self.device, ctypes.c_void_p(self.cache.base), ch, ctypes.byref(coff)),
+                        "kvx_ipc_export(kv cache)")
+            rec.cache_handle = ch.raw
+            rec.cache_offset = coff.value
+            rec.cache_ptr = self.cache.base
+            rec.cache_geometry = self.cache.geometry()
+        return rec
+
+    def export_buffer(self, ptr: int) -> tuple[bytes, int]:
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _capi.check(self.lib.kvx_ipc_export(self.device, ctypes.c_void_p(ptr), handle, ctypes.byref(off)),
+                    "kvx_ipc_export")
+        return handle.raw, off.value
+
+    def map_buffer(self, rec_pid: int, rec_device: int, handle: bytes, offset: int, ptr: int,
+                   closers: list | None) -> int:
+        """Address of a peer buffer usable from this GPU.
+
+        Other processes' buffers are opened through CUDA IPC once per
+        allocation (two buffers of one allocator segment share a handle) and
+        reference-counted; ``closers`` receives the handle to release.
+        """
+        if rec_pid == os.getpid():
+            if rec_device != self.device:
+                _capi.check(self.lib.kvx_enable_peer_access(self.device, rec_device), "kvx_enable_peer_access")
+            return int(ptr)
+        key = bytes(handle)
+        entry = self._ipc_maps.get(key)
+        if entry is None:
+            out = ctypes.c_uint64(0)
+            _capi.check(self.lib.kvx_ipc_open(self.device, key, 0, ctypes.byref(out)), "kvx_ipc_open")
+            entry = [int(out.value), 0]
+            self._ipc_maps[key] = entry
+        entry[1] += 1
+        if closers is not None:
+            closers.append(key)
+        return entry[0] + int(offset)
+
+    def unmap_buffer(self, key: bytes) -> None:
+        entry = self._ipc_maps.get(key)
+        if entry is None:
+            return
+        entry[1] -= 1
+        if entry[1] <= 0:
+            del self._ipc_maps[key]
+            _capi.check(self.lib.kvx_ipc_close(self.device, entry[0], 0), "kvx_ipc_close")
+
+    def link(self, rec: PeerRecord) -> PeerLink:
+        """Map a peer's mailbox and KV cache (idempotent)."""
+        with self._lock:
+            if rec.rank in self.links:
+                return self.links[rec.rank]
+            if rec.rank == self.rank:
+                raise RuntimeError("a rank does not link to itself")
+            if rec.mailbox_peers != self.world_size:
+                raise RuntimeError(f"peer {rec.rank} mailbox is for {rec.mailbox_peers} ranks, expected "
+                                   f"{self.world_size}")
+            if rec.pid != os.getpid():
+                ok = ctypes.c_int32(0)
+                _capi.check(self.lib.kvx_can_access_peer(self.device, rec.device, ctypes.byref(ok)),
+                            "kvx_can_access_peer")
+                if not ok.value:
+                    raise RuntimeError(f"cuda:{self.device} cannot access peer cuda:{rec.device} over NVLink/P2P")
+            closers: list = []
+            mb_ptr = self.map_buffer(rec.pid, rec.device, rec.mailbox_handle, rec.mailbox_offset, rec.mailbox_ptr,
+                                     closers)
+            mailbox = _capi.Mailbox(base=mb_ptr, max_peers=rec.mailbox_peers, reserved=0,
+                                    max_blocks=rec.mailbox_max_blocks)
+            cache = None
+            if rec.cache_geometry is not None:
+                base = self.map_buffer(rec.pid, rec.device, rec.cache_handle, rec.cache_offset, rec.cache_ptr,
+                                       closers)
+                g = rec.cache_geometry
+                cache = CacheLayout(base=base, kv_stride=g["kv_stride"], layer_stride=g["layer_stride"],
+                                    block_stride=g["block_stride"], num_blocks=g["num_blocks"],
+                                    chunk_bytes=g["chunk_bytes"], num_layers=g["num_layers"],
+                                    dtype=_dtype_from_name(g.get("dtype", "torch.uint8")),
+                                    device=torch.device("cuda", rec.device), block_shape=tuple(g["block_shape"]))
+            link = PeerLink(peer=rec.rank, mailbox=mailbox, cache=cache, closers=closers)
+            self.links[rec.rank] = link
+            return link
+
+    def get_link(self, peer: int) -> PeerLink:
+        link = self.links.get(int(peer))
+        if link is None:
+            raise RuntimeError(
+                f"rank {self.rank} has no mapping of rank {peer}: call prewarm_p2p_pairs "
+                "(every rank, after register_kv_cache) before transferring"
+            )
+        if link.poisoned:
+            raise RuntimeError(f"pair ({self.rank}, {peer}) is disabled after an earlier failure: {link.poisoned}")
+        return link
+
+    def next_token(self, src_rank: int) -> int:
+        with self._lock:
+            t = self.tokens_issued.get(src_rank, 0) + 1
+            self.tokens_issued[src_rank] = t
+            return t
+
+    # -- protocol steps (enqueue only) ----------------------------------------
+    def publish(self, link: PeerLink, dst_ids: torch.Tensor, num_ids: int, token: int, stream) -> None:
+        _capi.check(self.lib.kvx_pair_publish(self.device, ctypes.byref(link.mailbox), self.rank,
+                                              ctypes.c_void_p(dst_ids.data_ptr() if num_ids else 0), num_ids, token,
+                                              ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_pair_publish")
+
+    def wait_done(self, src_rank: int, token: int, timeout_s: float | None, stream) -> None:
+        _capi.check(self.lib.kvx_pair_wait_done(self.device, ctypes.byref(self.mailbox), src_rank, token,
+                                                timeout_ns(timeout_s), ctypes.c_void_p(self.status.data_ptr()),
+                                                ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_pair_wait_done")
+
+    def wait_armed(self, link: PeerLink, num_ids: int, timeout_s: float | None, stream) -> None:
+        _capi.check(self.lib.kvx_pair_wait_armed(self.device, ctypes.byref(self.mailbox), ctypes.byref(link.mailbox),
+                                                 self.rank, link.peer, num_ids, timeout_ns(timeout_s),
+                                                 ctypes.c_void_p(self.status.data_ptr()),
+                                                 ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_pair_wait_armed")
+
+    def push(self, src: CacheLayout, targets: list[tuple[PeerLink, CacheLayout, torch.Tensor, int]], stream) -> None:
+        """One launch per group of up to 8 targets: (link, peer layout, src ids, count)."""
+        for start in range(0, len(targets), MAX_TARGETS_PER_LAUNCH):
+            group = targets[start:start + MAX_TARGETS_PER_LAUNCH]
+            arr = (_capi.PushTarget * len(group))()
+            for k, (link, peer_layout, ids, n) in enumerate(group):
+                arr[k].dst = peer_layout.desc()
+                arr[k].dst_mailbox = link.mailbox
+                arr[k].src_ids_dev = ids.data_ptr() if n else 0
+                arr[k].num_ids = n
+                arr[k].dst_rank = link.peer
+                arr[k].reserved = 0
+            src_desc = src.desc()
+            _capi.check(self.lib.kvx_pair_push(self.device, ctypes.byref(src_desc), ctypes.byref(self.mailbox),
+                                               self.rank, arr, len(group), ctypes.c_void_p(self.status.data_ptr()),
+                                               ctypes.c_void_p(_capi.stream_handle(stream))),
+                        "kvx_pair_push")
+
+    def read_done(self, src_rank: int) -> int:
+        out = ctypes.c_uint64(0)
+        _capi.check(self.lib.kvx_mailbox_read_done(self.device, ctypes.byref(self.mailbox), src_rank,
+                                                   ctypes.byref(out)), "kvx_mailbox_read_done")
+        return out.value
+
+    def check_status(self, stream, what: str, peers=()) -> None:
+        stream.synchronize()
+        bits = int(self.status.item())
+        if bits:
+            if bits & (_capi.DEV_TIMEOUT | _capi.DEV_PIPE_TIMEOUT):
+                # A peer that is merely late may still write into blocks this
+                # rank is about to give back; refuse further use of the pair.
+                for p in peers:
+                    if p in self.links:
+                        self.links[p].poisoned = f"{what}: {_capi.describe_device_status(bits)}"
+            raise _capi.KvxError(f"{what} failed on rank {self.rank}: {_capi.describe_device_status(bits)}",
+                                 status=_capi.KVX_EINVAL, device_bits=bits)
+
+    def close_links(self) -> None:
+        """Release every peer mapping (the peers' memory stays theirs)."""
+        for link in self.links.values():
+            for key in link.closers:
+                try:
+                    self.unmap_buffer(key)
+                except Exception as exc:  # noqa: BLE001 - best effort at shutdown
+                    logger.warning("closing peer mapping failed: %s", exc)
+            link.closers = []
+        self.links.clear()
+
+    def close(self) -> None:
+        if self.closed:
+            return
+        for link in self.links.values():
+            for key in link.closers:
+                try:
+                    self.unmap_buffer(key)
+                except Exception as exc:  # noqa: BLE001 - best effort at shutdown
+                    logger.warning("closing peer mapping failed: %s", exc)
+        self.links.clear()
+        try:
+            _capi.check(self.lib.kvx_mailbox_destroy(self.device, ctypes.byref(self.mailbox)), "kvx_mailbox_destroy")
+        finally:
+            self.closed = True

@@ -1,0 +1,746 @@
+"""Drop-in replacement for ``lmpool.engine.kv_transfer`` on B200.
+
+Same names, arguments, return values and error behaviour as the reference
+module (src/lmpool/engine/kv_transfer.py), with the bytes moved by the
+sm_100a kernels of ``_kvx.so`` instead of ``index_select`` / NCCL
+``send``/``recv`` / ``index_copy_``:
+
+* ``_pack_all_layer_blocks`` / ``_unpack_all_layer_blocks`` (and the
+  per-layer helpers) are one kernel launch each over all layers, K/V planes
+  and blocks.
+* ``swap_in(..., negotiate_blocks=False)`` -- the planned path the data plane
+  uses (model_runner.py:747-806) -- has no staging payload and no NCCL call:
+  the source reads its blocks from HBM and stores them straight into the
+  destination's reserved blocks over NVLink (CUDA IPC mapping), then
+  release-stores a completion token the destination waits for (bounded).
+* ``prewarm_p2p_pairs`` maps every peer's KV cache and mailbox once (IPC
+  handles exchanged with one ``all_gather_object`` on the world group, all
+  ranks in the same order as the reference's group creation) and times one
+  transfer per pair, returning the same observation dicts.
+
+Additions with no reference counterpart: ``register_kv_cache`` (the cache to
+export; the reference allocates its payloads instead), ``move_blocks`` (a
+local gather+scatter in one launch), ``swap_batch`` (several directions at
+once without deadlock) and ``check_device_status``.
+
+There is no CPU path: CPU tensors raise ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import logging
+import os
+import socket
+import time
+from typing import Iterable, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _capi
+from .endpoint import PeerRecord, TransferEndpoint
+from .layout import (
+    CacheLayout,
+    affine_layout,
+    cache_layouts,
+    get_layer_kv,
+    payload_layout,
+)
+
+logger = logging.getLogger(__name__)
+
+# Same name as the reference; values are peer links (mapped mailbox + cache)
+# instead of NCCL process groups.
+_P2P_GROUPS: dict[tuple[int, int], object] = {}
+_ENDPOINTS: dict[int, TransferEndpoint] = {}
+_REGISTERED: dict[int, tuple[CacheLayout, object]] = {}
+_STATUS: dict[int, torch.Tensor] = {}
+
+
+# ---------------------------------------------------------------------------
+# Reference helpers kept with the same behaviour
+# ---------------------------------------------------------------------------
+
+def _normalize_transfer_pairs(pairs: Iterable[tuple[int, int]], world_size: int) -> list[tuple[int, int]]:
+    """kv_transfer.py:23-33: sorted, deduplicated, in-range pairs of distinct ranks."""
+    normalized = set()
+    for raw_a, raw_b in pairs:
+        a, b = sorted((int(raw_a), int(raw_b)))
+        if a == b or a < 0 or b >= world_size:
+            continue
+        normalized.add((a, b))
+    return sorted(normalized)
+
+
+def _pair_group(first: int, second: int):
+    """kv_transfer.py:36-37: the pair's link, or None if it was not prewarmed."""
+    return _P2P_GROUPS.get(tuple(sorted((int(first), int(second)))))
+
+
+def _allocate_empty_block(kv_cache: torch.Tensor, block_id: int) -> torch.Tensor:
+    """kv_transfer.py:125-138: a view of one block (no allocation)."""
+    return kv_cache[:, block_id, ...]
+
+
+def _compute_tag(block_id: int, layer_idx: int, is_k: bool) -> int:
+    """kv_transfer.py:141-146. Kept for API parity; the NVLink path has no tags."""
+    return block_id * 10000 + layer_idx * 2 + (0 if is_k else 1)
+
+
+_get_layer_kv = get_layer_kv
+
+
+# ---------------------------------------------------------------------------
+# Device plumbing
+# ---------------------------------------------------------------------------
+
+def _require_cuda(t: torch.Tensor, what: str) -> int:
+    if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+        raise RuntimeError(f"{what} must be a CUDA tensor: the B200 KV data path has no CPU implementation")
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def _status_word(device: int) -> torch.Tensor:
+    """Sticky per-device status word of the asynchronous helpers."""
+    st = _STATUS.get(device)
+    if st is None:
+        st = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", device))
+        _STATUS[device] = st
+    return st
+
+
+def check_device_status(device: int | None = None, reset: bool = True) -> int:
+    """Raise if a pack/unpack/store kernel on ``device`` flagged bad input.
+
+    Those launches never synchronise (CUDA-graph friendly); kernels OR their
+    failures into a per-device word this function reads (one device sync).
+    """
+    device = torch.cuda.current_device() if device is None else int(device)
+    st = _status_word(device)
+    torch.cuda.synchronize(device)
+    bits = int(st.item())
+    if reset and bits:
+        st.zero_()
+    if bits:
+        raise _capi.KvxError(f"KV kernel reported: {_capi.describe_device_status(bits)}", device_bits=bits)
+    return bits
+
+
+def _ids_tensor(ids: List[int], device: int) -> torch.Tensor:
+    host = torch.tensor([int(b) for b in ids], dtype=torch.int64)
+    if len(ids) == 0:
+        return host.to(torch.device("cuda", device))
+    return host.pin_memory().to(torch.device("cuda", device), non_blocking=True)
+
+
+def _validate(ids: List[int], num_blocks: int, distinct: bool, what: str) -> None:
+    lib = _capi.lib()
+    arr = (_capi.ctypes.c_int64 * max(1, len(ids)))(*[int(b) for b in ids])
+    rc = lib.kvx_validate_block_ids(arr, len(ids), int(num_blocks), 1 if distinct else 0)
+    if rc != _capi.KVX_OK:
+        raise RuntimeError(f"{what}: {_capi.last_error()}")
+
+
+def _launch_move(device: int, src: CacheLayout, dst: CacheLayout, src_ids: torch.Tensor | None,
+                 dst_ids: torch.Tensor | None, n: int, status: torch.Tensor, stream) -> None:
+    lib = _capi.lib()
+    sd, dd = src.desc(), dst.desc()
+    _capi.check(
+        lib.kvx_move_blocks(device, _capi.ctypes.byref(sd), _capi.ctypes.byref(dd),
+                            _capi.ctypes.c_void_p(src_ids.data_ptr() if src_ids is not None else 0),
+                            _capi.ctypes.c_void_p(dst_ids.data_ptr() if dst_ids is not None else 0), n,
+                            _capi.ctypes.c_void_p(status.data_ptr()),
+                            _capi.ctypes.c_void_p(_capi.stream_handle(stream))),
+        "kvx_move_blocks")
+
+
+def _layer_slice(lay: CacheLayout, layer: int) -> CacheLayout:
+    return CacheLayout(base=lay.base + layer * lay.layer_stride, kv_stride=lay.kv_stride, layer_stride=0,
+                       block_stride=lay.block_stride, num_blocks=lay.num_blocks, chunk_bytes=lay.chunk_bytes,
+                       num_layers=1, dtype=lay.dtype, device=lay.device, block_shape=lay.block_shape)
+
+
+def _move_layouts(device: int, src_lays: list[CacheLayout], dst_lays: list[CacheLayout], src_ids, dst_ids, n: int,
+                  num_layers: int, stream) -> None:
+    """Launch moves between two lists of layouts covering ``num_layers`` layers.
+
+    One launch when both sides are affine; one per layer otherwise. A
+    destination whose layers all alias one tensor (layer stride 0, e.g. a
+    5-D single-layer cache) keeps only the last layer's bytes, as the
+    reference's sequential per-layer copies leave it.
+    """
+    status = _status_word(device)
+    if len(src_lays) == 1 and len(dst_lays) == 1:
+        s, d = src_lays[0], dst_lays[0]
+        if d.layer_stride == 0 and num_layers > 1:
+            _launch_move(device, _layer_slice(s, num_layers - 1), _layer_slice(d, 0), src_ids, dst_ids, n, status,
+                         stream)
+            return
+        _launch_move(device, s, d, src_ids, dst_ids, n, status, stream)
+        return
+    for layer in range(num_layers):
+        s = src_lays[0] if len(src_lays) == 1 else src_lays[layer]
+        d = dst_lays[0] if len(dst_lays) == 1 else dst_lays[layer]
+        s1 = _layer_slice(s, layer) if s.num_layers > 1 else s
+        d1 = _layer_slice(d, layer) if d.num_layers > 1 else d
+        _launch_move(device, s1, d1, src_ids, dst_ids, n, status, stream)
+
+
+# ---------------------------------------------------------------------------
+# Pack / unpack (kv_transfer.py:180-276)
+# ---------------------------------------------------------------------------
+
+def _pack_layer_blocks(layer_k: torch.Tensor, layer_v: torch.Tensor, block_ids: List[int]) -> torch.Tensor:
+    """kv_transfer.py:180-196: one layer's K/V blocks -> contiguous [2, B, ...]."""
+    if not block_ids:
+        return torch.empty((2, 0, *layer_k.shape[1:]), dtype=layer_k.dtype, device=layer_k.device)
+    device = _require_cuda(layer_k, "layer_k")
+    src = cache_layouts((layer_k, layer_v), 1)
+    _validate(block_ids, src[0].num_blocks, False, "pack")
+    payload = torch.empty((2, len(block_ids), *layer_k.shape[1:]), dtype=layer_k.dtype, device=layer_k.device)
+    dst = payload_layout(1, len(block_ids), layer_k.shape[1:], layer_k.dtype, layer_k.device, payload.data_ptr())
+    ids = _ids_tensor(block_ids, device)
+    _move_layouts(device, src, [dst], ids, None, len(block_ids), 1, torch.cuda.current_stream(device))
+    return payload
+
+
+def _unpack_layer_blocks(payload: torch.Tensor, layer_k: torch.Tensor, layer_v: torch.Tensor,
+                         block_ids: List[int]) -> None:
+    """kv_transfer.py:199-215: scatter [2, B, ...] into destination blocks."""
+    if payload.shape[0] != 2 or payload.shape[1] != len(block_ids):
+        raise RuntimeError(
+            "packed KV payload does not match destination block count: "
+            f"payload={tuple(payload.shape)} blocks={len(block_ids)}"
+        )
+    if not block_ids:
+        return
+    device = _require_cuda(layer_k, "layer_k")
+    dst = cache_layouts((layer_k, layer_v), 1)
+    _validate(block_ids, dst[0].num_blocks, True, "unpack")
+    payload = payload.contiguous()
+    src = payload_layout(1, len(block_ids), payload.shape[2:], payload.dtype, payload.device, payload.data_ptr())
+    ids = _ids_tensor(block_ids, device)
+    _move_layouts(device, [src], dst, None, ids, len(block_ids), 1, torch.cuda.current_stream(device))
+
+
+def _empty_layer_payload(layer_k: torch.Tensor, num_blocks: int) -> torch.Tensor:
+    """kv_transfer.py:218-226."""
+    return torch.empty((2, num_blocks, *layer_k.shape[1:]), dtype=layer_k.dtype, device=layer_k.device)
+
+
+def _pack_all_layer_blocks(kv_cache, num_layers: int, block_ids: List[int]) -> torch.Tensor:
+    """kv_transfer.py:229-248: all layers' K/V blocks -> contiguous [L, 2, B, ...], one launch."""
+    first_k, _ = get_layer_kv(kv_cache, 0)
+    payload = torch.empty((num_layers, 2, len(block_ids), *first_k.shape[1:]), dtype=first_k.dtype,
+                          device=first_k.device)
+    if not block_ids:
+        return payload
+    device = _require_cuda(first_k, "kv_cache")
+    src = cache_layouts(kv_cache, num_layers)
+    _validate(block_ids, src[0].num_blocks, False, "pack")
+    dst = payload_layout(num_layers, len(block_ids), first_k.shape[1:], first_k.dtype, first_k.device,
+                         payload.data_ptr())
+    ids = _ids_tensor(block_ids, device)
+    _move_layouts(device, src, [dst], ids, None, len(block_ids), num_layers, torch.cuda.current_stream(device))
+    return payload
+
+
+def _empty_all_layer_payload(kv_cache, num_layers: int, num_blocks: int) -> torch.Tensor:
+    """kv_transfer.py:251-261."""
+    first_k, _ = get_layer_kv(kv_cache, 0)
+    return torch.empty((num_layers, 2, num_blocks, *first_k.shape[1:]), dtype=first_k.dtype, device=first_k.device)
+
+
+def _unpack_all_layer_blocks(payload: torch.Tensor, kv_cache, block_ids: List[int]) -> None:
+    """kv_transfer.py:264-276: scatter [L, 2, B, ...] into destination blocks, one launch."""
+    if payload.shape[0] <= 0 or payload.shape[2] != len(block_ids):
+        raise RuntimeError(
+            "packed multi-layer KV payload does not match destination blocks: "
+            f"payload={tuple(payload.shape)} blocks={len(block_ids)}"
+        )
+    num_layers = int(payload.shape[0])
+    first_k, _ = get_layer_kv(kv_cache, 0)
+    if not block_ids:
+        return
+    device = _require_cuda(first_k, "kv_cache")
+    dst = cache_layouts(kv_cache, num_layers)
+    _validate(block_ids, dst[0].num_blocks, True, "unpack")
+    payload = payload.contiguous()
+    src = payload_layout(num_layers, len(block_ids), payload.shape[3:], payload.dtype, payload.device,
+                         payload.data_ptr())
+    ids = _ids_tensor(block_ids, device)
+    _move_layouts(device, [src], dst, None, ids, len(block_ids), num_layers, torch.cuda.current_stream(device))
+
+
+def move_blocks(kv_cache, num_layers: int, src_blocks: List[int], dst_blocks: List[int],
+                dst_kv_cache=None, stream=None, synchronize: bool = False) -> List[int]:
+    """Local gather+scatter: ``dst_cache[:, :, dst_blocks[i]] = src_cache[:, :, src_blocks[i]]``.
+
+    The same result as ``_unpack_all_layer_blocks(_pack_all_layer_blocks(...))``
+    (kv_transfer.py:229-276) in ONE launch without a payload, when source and
+    destination chunks are disjoint; overlapping ids on the same cache go
+    through a payload (two launches) so the result stays that of the
+    reference. Returns ``list(dst_blocks)``.
+    """
+    if len(src_blocks) != len(dst_blocks):
+        raise RuntimeError(f"move_blocks: {len(src_blocks)} source ids but {len(dst_blocks)} destination ids")
+    dst_kv_cache = kv_cache if dst_kv_cache is None else dst_kv_cache
+    if not src_blocks:
+        return []
+    first_k, _ = get_layer_kv(kv_cache, 0)
+    device = _require_cuda(first_k, "kv_cache")
+    src = cache_layouts(kv_cache, num_layers)
+    dst = cache_layouts(dst_kv_cache, num_layers)
+    _validate(src_blocks, src[0].num_blocks, False, "move_blocks source")
+    _validate(dst_blocks, dst[0].num_blocks, True, "move_blocks destination")
+    stream = torch.cuda.current_stream(device) if stream is None else stream
+    same = [s.base for s in src] == [d.base for d in dst]
+    if same:
+        overlap = bool(set(int(b) for b in src_blocks) & set(int(b) for b in dst_blocks))
+    else:
+        overlap = False
+    with torch.cuda.stream(stream):
+        if overlap:
+            payload = _pack_all_layer_blocks(kv_cache, num_layers, src_blocks)
+            _unpack_all_layer_blocks(payload, dst_kv_cache, dst_blocks)
+        else:
+            sid = _ids_tensor(src_blocks, device)
+            did = _ids_tensor(dst_blocks, device)
+            _move_layouts(device, src, dst, sid, did, len(src_blocks), num_layers, stream)
+    if synchronize:
+        check_device_status(device)
+    return list(dst_blocks)
+
+
+# ---------------------------------------------------------------------------
+# Cross-GPU path
+# ---------------------------------------------------------------------------
+
+def _local_device(rank: int) -> int:
+    if "LOCAL_RANK" in os.environ:
+        return int(os.environ["LOCAL_RANK"])
+    n = torch.cuda.device_count()
+    return rank % n if n else rank
+
+
+def _num_layers_of(kv_cache) -> int:
+    if isinstance(kv_cache, (list, tuple)) and kv_cache and isinstance(kv_cache[0], (list, tuple)):
+        return len(kv_cache)
+    if isinstance(kv_cache, torch.Tensor) and kv_cache.dim() == 6:
+        return int(kv_cache.shape[1])
+    return 1
+
+
+def register_kv_cache(kv_cache, num_layers: int | None = None) -> CacheLayout:
+    """Declare this rank's KV cache so prewarm can export it to peers.
+
+    Call once after ``ModelRunner.allocate_kv_cache`` (model_runner.py:397-406)
+    and before ``prewarm_p2p_pairs``. The cache must be one allocation made
+    with cudaMalloc (PyTorch's default allocator; not expandable segments).
+    """
+    num_layers = _num_layers_of(kv_cache) if num_layers is None else int(num_layers)
+    first_k, _ = get_layer_kv(kv_cache, 0)
+    device = _require_cuda(first_k, "kv_cache")
+    lay = affine_layout(kv_cache, num_layers)
+    _REGISTERED[device] = (lay, kv_cache)
+    ep = _ENDPOINTS.get(device)
+    if ep is not None and ep.cache is not None and ep.cache.base != lay.base:
+        raise RuntimeError("a different KV cache is already mapped by peers; restart the pair setup")
+    return lay
+
+
+def _endpoint(rank: int, world_size: int, device: int, max_blocks: int) -> TransferEndpoint:
+    ep = _ENDPOINTS.get(device)
+    if ep is not None and (ep.rank != rank or ep.world_size != world_size or ep.mailbox.max_blocks < max_blocks):
+        raise RuntimeError("transfer endpoint was set up for another world; call shutdown() first")
+    if ep is None:
+        ep = TransferEndpoint(rank, world_size, device, max_blocks)
+        _ENDPOINTS[device] = ep
+    return ep
+
+
+def shutdown(barrier: bool = True) -> None:
+    """Close peer mappings, then free mailboxes (tests, orderly exit).
+
+    With a process group, every rank unmaps its peers before any rank frees
+    its own mailbox (a collective: all ranks call it together).
+    """
+    for ep in list(_ENDPOINTS.values()):
+        ep.close_links()
+    if barrier and dist.is_available() and dist.is_initialized():
+        dist.barrier()
+    for ep in list(_ENDPOINTS.values()):
+        ep.close()
+    _ENDPOINTS.clear()
+    _P2P_GROUPS.clear()
+
+
+def prewarm_p2p_pairs(
+    pairs: Iterable[tuple[int, int]],
+    *,
+    num_layers: int = 1,
+    block_size: int = 1,
+    num_kv_heads: int = 1,
+    head_dim: int = 1,
+    num_blocks: int = 1,
+    dtype: torch.dtype | None = None,
+    kv_cache=None,
+    timeout_s: float | None = None,
+) -> list[dict]:
+    """kv_transfer.py:40-119: set up every pair once and time one transfer per pair.
+
+    All world ranks call this in the same order (it runs world collectives).
+    Each rank exports its mailbox and registered KV cache; every rank maps
+    every peer it can reach (NVSwitch makes all pairs direct), so the
+    ``pairs`` list only selects which pairs get a timed warm transfer of a
+    ``[L, 2, num_blocks, block_size, H, D]`` payload filled with ``src + 1``,
+    checked on the destination. Returns the source ranks' observations
+    ``{src_gpu, dst_gpu, transfer_bytes, transfer_time_s}``.
+    """
+    if not dist.is_available() or not dist.is_initialized():
+        return []
+    rank = dist.get_rank()
+    world_size = dist.get_world_size()
+    device = _local_device(rank)
+    torch.cuda.set_device(device)
+    normalized = _normalize_transfer_pairs(pairs, world_size)
+    if kv_cache is not None:
+        register_kv_cache(kv_cache, num_layers)
+    reg = _REGISTERED.get(device)
+    payload_shape = (max(1, int(num_layers)), 2, max(1, int(num_blocks)), max(1, int(block_size)),
+                     max(1, int(num_kv_heads)), max(1, int(head_dim)))
+    # Capacity of each per-peer id slot: the largest cache in the world.
+    own_n = max(reg[0].num_blocks if reg else 1, payload_shape[2])
+    sizes: list = [None] * world_size
+    dist.all_gather_object(sizes, own_n)
+    ep = _endpoint(rank, world_size, device, max(int(s) for s in sizes))
+    if reg is not None and ep.cache is None:
+        ep.set_cache(reg[0], keepalive=reg[1])
+
+    payload = torch.empty(payload_shape, dtype=dtype or torch.get_default_dtype(), device=torch.device("cuda", device))
+    pl_layout = payload_layout(payload_shape[0], payload_shape[2], payload_shape[3:], payload.dtype, payload.device,
+                               payload.data_ptr())
+    rec = ep.export_record(hostname=socket.gethostname())
+    pl_handle, pl_off = ep.export_buffer(payload.data_ptr())
+    rec.extra = {"payload_handle": pl_handle, "payload_offset": pl_off, "payload_ptr": payload.data_ptr()}
+    records: list = [None] * world_size
+    dist.all_gather_object(records, rec)
+
+    payload_maps: dict[int, CacheLayout] = {}
+    payload_closers: list = []
+    for other in records:
+        if other.rank == rank or other.hostname != rec.hostname:
+            continue
+        link = ep.link(other)
+        ptr = ep.map_buffer(other.pid, other.device, other.extra["payload_handle"], other.extra["payload_offset"],
+                            other.extra["payload_ptr"], payload_closers)
+        payload_maps[other.rank] = pl_layout.with_base(ptr)
+        pair = tuple(sorted((rank, other.rank)))
+        _P2P_GROUPS[pair] = link
+    dist.barrier()
+
+    observations = []
+    stream = torch.cuda.current_stream(device)
+    ids = list(range(payload_shape[2]))
+    for src, dst in normalized:
+        payload.fill_(float(src + 1) if rank == src else 0.0)
+        # Warm-up transfer: first touch of the peer mapping and kernels.
+        if rank == src:
+            _source_side(ep, dst, pl_layout, payload_maps[dst], ids, timeout_s, stream)
+        elif rank == dst:
+            _destination_side(ep, src, ids, len(ids), timeout_s, stream)
+        dist.barrier()
+        if rank == src:
+            torch.cuda.synchronize(device)
+            started = time.perf_counter()
+            _source_side(ep, dst, pl_layout, payload_maps[dst], ids, timeout_s, stream)
+            torch.cuda.synchronize(device)
+            observations.append({
+                "src_gpu": src,
+                "dst_gpu": dst,
+                "transfer_bytes": payload.numel() * payload.element_size(),
+                "transfer_time_s": time.perf_counter() - started,
+            })
+        elif rank == dst:
+            payload.fill_(0.0)
+            _destination_side(ep, src, ids, len(ids), timeout_s, stream)
+            if not bool(torch.all(payload == float(src + 1)).item()):
+                raise RuntimeError(f"KV transfer P2P prewarm validation failed for pair {(src, dst)}")
+        dist.barrier()
+    # Peers unmap this rank's payload before it is freed.
+    for key in payload_closers:
+        ep.unmap_buffer(key)
+    dist.barrier()
+    del payload
+    return observations
+
+
+def _destination_side(ep: TransferEndpoint, src_rank: int, dst_ids: List[int], expected: int,
+                      timeout_s: float | None, stream) -> None:
+    link = ep.get_link(src_rank)
+    token = ep.next_token(src_rank)
+    ids = _ids_tensor(dst_ids, ep.device)
+    with torch.cuda.stream(stream):
+        ep.status.zero_()
+    ep.publish(link, ids, len(dst_ids), token, stream)
+    ep.wait_done(src_rank, token, timeout_s, stream)
+    ep.check_status(stream, f"transfer {src_rank}->{ep.rank} (destination)", peers=(src_rank,))
+
+
+def _source_side(ep: TransferEndpoint, dst_rank: int, local: CacheLayout, remote: CacheLayout, src_ids: List[int],
+                 timeout_s: float | None, stream) -> None:
+    link = ep.get_link(dst_rank)
+    ids = _ids_tensor(src_ids, ep.device)
+    with torch.cuda.stream(stream):
+        ep.status.zero_()
+    ep.wait_armed(link, len(src_ids), timeout_s, stream)
+    ep.push(local, [(link, remote, ids, len(src_ids))], stream)
+    ep.check_status(stream, f"transfer {ep.rank}->{dst_rank} (source)", peers=(dst_rank,))
+
+
+def _check_registered(ep: TransferEndpoint, kv_cache, num_layers: int) -> None:
+    if ep.cache is None:
+        raise RuntimeError("no KV cache registered on this rank: call register_kv_cache before prewarm_p2p_pairs")
+    lay = affine_layout(kv_cache, num_layers)
+    if (lay.base, lay.kv_stride, lay.layer_stride, lay.block_stride, lay.num_layers) != (
+            ep.cache.base, ep.cache.kv_stride, ep.cache.layer_stride, ep.cache.block_stride, ep.cache.num_layers):
+        raise RuntimeError("kv_cache passed to swap_in is not the cache registered for peer mapping")
+
+
+def swap_in(
+    remote_gpu: int,
+    remote_blocks: List[int],
+    local_gpu: int,
+    kv_cache: torch.Tensor,
+    num_layers: int,
+    block_size: int,
+    num_kv_heads: int,
+    head_dim: int,
+    local_target_blocks: Optional[List[int]] = None,
+    negotiate_blocks: bool = True,
+    timeout_s: float | None = None,
+) -> List[int]:
+    """kv_transfer.py:395-475: move ``remote_blocks`` of ``remote_gpu`` into ``local_gpu``.
+
+    Called by both ranks of the pair (ModelRunner.execute_swap_out on the
+    source, execute_swap_in on the destination, model_runner.py:747-806).
+    Returns the destination block ids on every rank (the source returns
+    ``list(remote_blocks)`` on the planned path, as the reference does).
+    Blocks until this rank's side is complete: on the destination, until the
+    blocks are in its cache; on the source, until its stores have landed.
+    """
+    logger.info("transfer_in: GPU%s -> GPU%s | blocks=%s", remote_gpu, local_gpu, remote_blocks)
+    rank = dist.get_rank()
+
+    if not negotiate_blocks:
+        if rank == local_gpu and rank != remote_gpu:
+            if local_target_blocks is None:
+                raise RuntimeError("planned transfer requires local_target_blocks")
+            local_blocks = list(local_target_blocks)
+        else:
+            local_blocks = list(remote_blocks)
+    elif rank == local_gpu and rank != remote_gpu:
+        _send_block_list(remote_blocks, dst=remote_gpu)
+        _send_block_list(list(local_target_blocks) if local_target_blocks is not None else [], dst=remote_gpu)
+        local_blocks = _recv_block_list(src=remote_gpu)
+    elif rank == remote_gpu and rank != local_gpu:
+        remote_blocks_recv = _recv_block_list(src=local_gpu)
+        specified = _recv_block_list(src=local_gpu)
+        local_blocks = specified if specified else remote_blocks_recv
+        _send_block_list(local_blocks, dst=local_gpu)
+    else:
+        local_blocks = remote_blocks
+
+    if len(local_blocks) != len(remote_blocks):
+        raise RuntimeError(
+            f"transfer_in negotiated mismatched block counts: "
+            f"remote={len(remote_blocks)} local={len(local_blocks)}"
+        )
+
+    if rank == local_gpu and rank != remote_gpu:
+        ep = _ENDPOINTS.get(_local_device(rank))
+        if ep is None:
+            raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
+        _check_registered(ep, kv_cache, num_layers)
+        _validate(local_blocks, ep.cache.num_blocks, True, "transfer destination")
+        _destination_side(ep, remote_gpu, local_blocks, len(remote_blocks), timeout_s,
+                          torch.cuda.current_stream(ep.device))
+    elif rank == remote_gpu and rank != local_gpu:
+        ep = _ENDPOINTS.get(_local_device(rank))
+        if ep is None:
+            raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
+        _check_registered(ep, kv_cache, num_layers)
+        _validate(remote_blocks, ep.cache.num_blocks, False, "transfer source")
+        link = ep.get_link(local_gpu)
+        if link.cache is None:
+            raise RuntimeError(f"rank {local_gpu} did not register a KV cache")
+        _source_side(ep, local_gpu, ep.cache, link.cache, list(remote_blocks), timeout_s,
+                     torch.cuda.current_stream(ep.device))
+    return local_blocks
+
+
+def swap_out(
+    local_gpu: int,
+    blocks_to_evict: List[int],
+    target_gpu: int,
+    kv_cache: torch.Tensor,
+    num_layers: int,
+    block_size: int,
+    num_kv_heads: int,
+    head_dim: int,
+    target_free_blocks: Optional[List[int]] = None,
+    timeout_s: float | None = None,
+) -> List[int]:
+    """kv_transfer.py:310-392 (legacy negotiated variant): move ``blocks_to_evict`` to ``target_gpu``.
+
+    Block ids are negotiated over the world group like the reference (source
+    sends its ids and the optional target list, destination answers with the
+    ids to use); the bytes then move with the NVLink push. An absent
+    ``target_free_blocks`` is sent as an empty list so both sides exchange
+    the same number of messages.
+    """
+    logger.info("transfer_out: GPU%s -> GPU%s | blocks=%s", local_gpu, target_gpu, blocks_to_evict)
+    rank = dist.get_rank()
+    if rank == local_gpu and rank != target_gpu:
+        _send_block_list(blocks_to_evict, dst=target_gpu)
+        _send_block_list(list(target_free_blocks) if target_free_blocks is not None else [], dst=target_gpu)
+        target_blocks = _recv_block_list(src=target_gpu)
+    elif rank == target_gpu and rank != local_gpu:
+        _recv_block_list(src=local_gpu)
+        specified = _recv_block_list(src=local_gpu)
+        target_blocks = specified if specified else []
+        _send_block_list(target_blocks, dst=local_gpu)
+    else:
+        target_blocks = blocks_to_evict
+    if len(target_blocks) != len(blocks_to_evict):
+        raise RuntimeError(
+            f"transfer_out negotiated mismatched block counts: "
+            f"src={len(blocks_to_evict)} dst={len(target_blocks)}"
+        )
+    if rank == local_gpu and rank != target_gpu:
+        ep = _ENDPOINTS.get(_local_device(rank))
+        if ep is None:
+            raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
+        _check_registered(ep, kv_cache, num_layers)
+        _validate(blocks_to_evict, ep.cache.num_blocks, False, "transfer source")
+        link = ep.get_link(target_gpu)
+        _source_side(ep, target_gpu, ep.cache, link.cache, list(blocks_to_evict), timeout_s,
+                     torch.cuda.current_stream(ep.device))
+    elif rank == target_gpu and rank != local_gpu:
+        ep = _ENDPOINTS.get(_local_device(rank))
+        if ep is None:
+            raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
+        _check_registered(ep, kv_cache, num_layers)
+        _validate(target_blocks, ep.cache.num_blocks, True, "transfer destination")
+        _destination_side(ep, local_gpu, target_blocks, len(blocks_to_evict), timeout_s,
+                          torch.cuda.current_stream(ep.device))
+    return target_blocks
+
+
+def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, List[int]]],
+               kv_cache=None, num_layers: int | None = None, timeout_s: float | None = None,
+               stream=None, synchronize: bool = True) -> None:
+    """Several transfers of this rank at once, in either direction.
+
+    ``outgoing`` = [(dst_rank, src_block_ids)], ``incoming`` =
+    [(src_rank, local_target_block_ids)]. Every incoming arm is published
+    before anything waits, and all outgoing transfers share one push launch
+    (up to 8 destinations per launch), so a rank that both sends and receives
+    cannot deadlock against its peers (two sequential ``swap_in`` calls in
+    opposite directions would: each source waits for its peer's arm).
+    """
+    device = _local_device(dist.get_rank())
+    ep = _ENDPOINTS.get(device)
+    if ep is None:
+        raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
+    if kv_cache is not None:
+        _check_registered(ep, kv_cache, num_layers if num_layers is not None else ep.cache.num_layers)
+    if ep.cache is None:
+        raise RuntimeError("no KV cache registered on this rank")
+    stream = torch.cuda.current_stream(device) if stream is None else stream
+    peers = []
+    with torch.cuda.stream(stream):
+        ep.status.zero_()
+    tokens = []
+    for src_rank, dst_ids in incoming:
+        _validate(dst_ids, ep.cache.num_blocks, True, "transfer destination")
+        link = ep.get_link(src_rank)
+        token = ep.next_token(src_rank)
+        ids = _ids_tensor(dst_ids, device)
+        ep.publish(link, ids, len(dst_ids), token, stream)
+        tokens.append((src_rank, token, ids))
+        peers.append(src_rank)
+    targets = []
+    for dst_rank, src_ids in outgoing:
+        _validate(src_ids, ep.cache.num_blocks, False, "transfer source")
+        link = ep.get_link(dst_rank)
+        if link.cache is None:
+            raise RuntimeError(f"rank {dst_rank} did not register a KV cache")
+        ep.wait_armed(link, len(src_ids), timeout_s, stream)
+        targets.append((link, link.cache, _ids_tensor(src_ids, device), len(src_ids)))
+        peers.append(dst_rank)
+    if targets:
+        ep.push(ep.cache, targets, stream)
+    for src_rank, token, _ids in tokens:
+        ep.wait_done(src_rank, token, timeout_s, stream)
+    if synchronize:
+        ep.check_status(stream, f"swap_batch on rank {ep.rank}", peers=peers)
+
+
+# ---------------------------------------------------------------------------
+# Legacy negotiation messages (kv_transfer.py:283-303) and free-block requests
+# (kv_transfer.py:482-524): host-side id lists over the world group.
+# ---------------------------------------------------------------------------
+
+def _p2p_device():
+    if dist.get_backend() == "nccl":
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cpu")
+
+
+def _send_block_list(blocks: List[int], dst: int) -> None:
+    dev = _p2p_device()
+    length = torch.tensor([len(blocks)], dtype=torch.int64, device=dev)
+    dist.send(length, dst=dst, tag=99999)
+    if len(blocks) > 0:
+        dist.send(torch.tensor(list(blocks), dtype=torch.int64, device=dev), dst=dst, tag=99998)
+
+
+def _recv_block_list(src: int) -> List[int]:
+    dev = _p2p_device()
+    length = torch.tensor([0], dtype=torch.int64, device=dev)
+    dist.recv(length, src=src, tag=99999)
+    n = int(length.item())
+    if n == 0:
+        return []
+    t = torch.zeros(n, dtype=torch.int64, device=dev)
+    dist.recv(t, src=src, tag=99998)
+    return t.tolist()
+
+
+def request_free_blocks(target_gpu: int, num_blocks: int) -> List[int]:
+    """kv_transfer.py:482-507 (legacy, no caller in LMPool)."""
+    rank = dist.get_rank()
+    if rank == target_gpu:
+        raise RuntimeError("request_free_blocks should not be called on target GPU directly")
+    dev = _p2p_device()
+    dist.send(torch.tensor([num_blocks], dtype=torch.int64, device=dev), dst=target_gpu, tag=88888)
+    n_tensor = torch.tensor([0], dtype=torch.int64, device=dev)
+    dist.recv(n_tensor, src=target_gpu, tag=88887)
+    n = int(n_tensor.item())
+    if n == 0:
+        return []
+    blocks = torch.zeros(n, dtype=torch.int64, device=dev)
+    dist.recv(blocks, src=target_gpu, tag=88886)
+    return blocks.tolist()
+
+
+def respond_free_blocks(requester_gpu: int, allocated_blocks: List[int]) -> None:
+    """kv_transfer.py:510-524 (legacy)."""
+    rank = dist.get_rank()
+    if rank != requester_gpu:
+        dev = _p2p_device()
+        n = len(allocated_blocks)
+        dist.send(torch.tensor([n], dtype=torch.int64, device=dev), dst=requester_gpu, tag=88887)
+        if n > 0:
+            dist.send(torch.tensor(list(allocated_blocks), dtype=torch.int64, device=dev), dst=requester_gpu,
+                      tag=88886)

@@ -1,0 +1,276 @@
+"""GPU tests of the pair protocol (publish -> wait_armed -> push -> wait_done).
+
+On one GPU, two endpoints (ranks 0 and 1) share the device and every step
+runs in order on ONE stream, so each bounded wait is satisfied by a kernel
+that finished before it started. On two GPUs the same protocol runs across
+NVLink, in one process (peer pointers) and in two processes (CUDA IPC,
+handles exchanged over gloo) through the public swap_in API.
+"""
+import ctypes
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from lmpool_b200 import _capi
+from lmpool_b200.endpoint import TransferEndpoint
+from lmpool_b200.layout import affine_layout
+from oracle import c_oracle
+from tests import kvgen
+from tests.conftest import device_count
+
+pytestmark = pytest.mark.gpu
+
+
+def _same_bits(a, b) -> bool:
+    a, b = a.detach().contiguous().cpu(), b.detach().contiguous().cpu()
+    return a.shape == b.shape and torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
+def _pair(dev0: int, dev1: int, shape, seed: int):
+    N = shape[2]
+    src_cpu = kvgen.seeded_cache(shape, seed)
+    dst_cpu = kvgen.seeded_cache(shape, seed + 1)
+    src = src_cpu.to(torch.device("cuda", dev0))
+    dst = dst_cpu.to(torch.device("cuda", dev1))
+    ep0 = TransferEndpoint(0, 2, dev0, N)
+    ep1 = TransferEndpoint(1, 2, dev1, N)
+    ep0.set_cache(affine_layout(src, shape[1]), src)
+    ep1.set_cache(affine_layout(dst, shape[1]), dst)
+    link01 = ep0.link(ep1.export_record())
+    link10 = ep1.link(ep0.export_record())
+    return src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10
+
+
+def _ids(ids, dev):
+    return torch.tensor(ids, dtype=torch.int64, device=torch.device("cuda", dev))
+
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])
+def test_loopback_protocol_on_one_stream(require_gpu, variant):
+    lib = require_gpu
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(ctypes.byref(old))
+    lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=variant)))
+    try:
+        shape = (2, 36, 24, 256, 8, 128)   # Qwen3-8B geometry, reduced N
+        src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 5)
+        s = torch.cuda.current_stream(0)
+        for round_ in range(3):             # tokens 1, 2, 3 on the same pair
+            src_ids = kvgen.seeded_perm(24, 50 + round_)[:8]
+            dst_ids = kvgen.seeded_perm(24, 60 + round_)[:8]
+            ep0.status.zero_()
+            ep1.status.zero_()
+            token = ep1.next_token(0)
+            assert token == round_ + 1
+            ep1.publish(link10, _ids(dst_ids, 0), 8, token, s)
+            ep0.wait_armed(link01, 8, 5.0, s)
+            ep0.push(ep0.cache, [(link01, link01.cache, _ids(src_ids, 0), 8)], s)
+            ep1.wait_done(0, token, 5.0, s)
+            ep0.check_status(s, "source")
+            ep1.check_status(s, "destination")
+            c_oracle.swap_planned(src_cpu, src_ids, dst_cpu, dst_ids, nthreads=4)
+            assert _same_bits(dst, dst_cpu)
+            assert _same_bits(src, src_cpu)
+            assert ep1.read_done(0) == token
+        ep0.close()
+        ep1.close()
+    finally:
+        lib.kvx_set_tuning(ctypes.byref(old))
+
+
+def test_wait_times_out_with_a_status_and_the_context_survives(require_gpu):
+    shape = (2, 2, 8, 16, 1, 64)
+    _, _, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 7)
+    s = torch.cuda.current_stream(0)
+    ep1.status.zero_()
+    t0 = time.perf_counter()
+    ep1.wait_done(0, 1, 0.2, s)          # nothing will ever signal token 1
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep1.check_status(s, "destination", peers=(0,))
+    assert time.perf_counter() - t0 < 30
+    assert link10.poisoned                # the pair refuses further use
+    with pytest.raises(RuntimeError, match="disabled"):
+        ep1.get_link(0)
+    ep0.status.zero_()
+    ep0.wait_armed(link01, 4, 0.2, s)    # no arm was ever posted
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep0.check_status(s, "source")
+    # the device still works
+    x = torch.arange(10, device="cuda:0")
+    assert int(x.sum().item()) == 45
+    ep0.close()
+    ep1.close()
+
+
+def test_stale_completion_cannot_satisfy_a_newer_transfer(require_gpu):
+    shape = (2, 2, 8, 16, 1, 64)
+    _, _, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 8)
+    s = torch.cuda.current_stream(0)
+    ids = _ids([1, 2], 0)
+    for e in (ep0, ep1):
+        e.status.zero_()
+    t1 = ep1.next_token(0)
+    ep1.publish(link10, ids, 2, t1, s)
+    ep0.wait_armed(link01, 2, 2.0, s)
+    ep0.push(ep0.cache, [(link01, link01.cache, ids, 2)], s)
+    ep1.wait_done(0, t1, 2.0, s)
+    ep1.check_status(s, "first")
+    t2 = ep1.next_token(0)                # destination arms again, source never pushes
+    ep1.publish(link10, ids, 2, t2, s)
+    ep1.wait_done(0, t2, 0.2, s)
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep1.check_status(s, "second")
+    ep0.close()
+    ep1.close()
+
+
+def test_count_mismatch_fails_both_sides_without_moving_data(require_gpu):
+    shape = (2, 2, 8, 16, 1, 64)
+    _, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 9)
+    s = torch.cuda.current_stream(0)
+    for e in (ep0, ep1):
+        e.status.zero_()
+    token = ep1.next_token(0)
+    ep1.publish(link10, _ids([0, 1, 2], 0), 3, token, s)
+    ep0.wait_armed(link01, 4, 2.0, s)                       # source moves 4, destination posted 3
+    ep0.push(ep0.cache, [(link01, link01.cache, _ids([4, 5, 6, 7], 0), 4)], s)
+    ep1.wait_done(0, token, 2.0, s)
+    with pytest.raises(_capi.KvxError, match="different block count"):
+        ep0.check_status(s, "source")
+    with pytest.raises(_capi.KvxError, match="peer reported failure"):
+        ep1.check_status(s, "destination")
+    assert _same_bits(dst, dst_cpu)
+    ep0.close()
+    ep1.close()
+
+
+@pytest.mark.skipif(device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])
+def test_two_gpus_one_process_push_over_nvlink(require_gpu, variant):
+    lib = require_gpu
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(ctypes.byref(old))
+    lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=variant)))
+    try:
+        shape = (2, 36, 64, 256, 8, 128)
+        src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 1, shape, 11)
+        s0, s1 = torch.cuda.current_stream(0), torch.cuda.current_stream(1)
+        src_ids = list(range(10, 26))                 # a contiguous run
+        dst_ids = kvgen.seeded_perm(64, 12)[:16]
+        ep0.status.zero_()
+        ep1.status.zero_()
+        token = ep1.next_token(0)
+        ep1.publish(link10, _ids(dst_ids, 1), 16, token, s1)
+        ep1.wait_done(0, token, 10.0, s1)
+        ep0.wait_armed(link01, 16, 10.0, s0)
+        ep0.push(ep0.cache, [(link01, link01.cache, _ids(src_ids, 0), 16)], s0)
+        ep0.check_status(s0, "source")
+        ep1.check_status(s1, "destination")
+        c_oracle.swap_planned(src_cpu, src_ids, dst_cpu, dst_ids, nthreads=8)
+        assert _same_bits(dst, dst_cpu)
+        ep0.close()
+        ep1.close()
+    finally:
+        lib.kvx_set_tuning(ctypes.byref(old))
+
+
+def _free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
+def _swap_worker(rank: int, port: int, queue) -> None:
+    import torch.distributed as dist
+
+    from lmpool_b200 import kv_transfer as kt
+
+    try:
+        torch.cuda.set_device(rank)
+        os.environ["LOCAL_RANK"] = str(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", world_size=2, rank=rank)
+        shape = (2, 4, 16, 2, 1, 8)
+        cache = torch.zeros(shape, dtype=torch.float32, device=f"cuda:{rank}")
+        kt.register_kv_cache(cache, 4)
+        obs = kt.prewarm_p2p_pairs([(0, 1)], num_layers=4, block_size=2, num_kv_heads=1, head_dim=8, num_blocks=2,
+                                   dtype=torch.float32, timeout_s=20)
+        # reference test (tests/test_kv_transfer.py:105-174): rank 0 blocks [0, 1] -> rank 1 blocks [2, 3]
+        if rank == 0:
+            cache[0, :, 0].fill_(1.0)
+            cache[1, :, 0].fill_(1.5)
+            cache[0, :, 1].fill_(2.0)
+            cache[1, :, 1].fill_(2.5)
+        dist.barrier()
+        got = kt.swap_in(remote_gpu=0, remote_blocks=[0, 1], local_gpu=1, kv_cache=cache, num_layers=4,
+                         block_size=2, num_kv_heads=1, head_dim=8,
+                         local_target_blocks=[2, 3] if rank == 1 else None, negotiate_blocks=False, timeout_s=20)
+        dist.barrier()
+        ok = got == ([0, 1] if rank == 0 else [2, 3])
+        if rank == 1:
+            ok &= bool((cache[0, :, 2] == 1.0).all() and (cache[1, :, 2] == 1.5).all())
+            ok &= bool((cache[0, :, 3] == 2.0).all() and (cache[1, :, 3] == 2.5).all())
+            ok &= bool(cache[:, :, [0, 1] + list(range(4, 16))].abs().sum().item() == 0)
+        # seeded bf16 transfer at Qwen3-8B geometry (reduced N), both directions in turn
+        big_shape = (2, 36, 32, 256, 8, 128)
+        for step, (s_rank, d_rank) in enumerate(((0, 1), (1, 0))):
+            src_ids = kvgen.seeded_perm(32, 100 + step)[:9]
+            dst_ids = kvgen.seeded_perm(32, 200 + step)[:9]
+            if step == 0:
+                big_cpu = kvgen.seeded_cache(big_shape, rank)
+                big = big_cpu.to(f"cuda:{rank}")
+                kt.shutdown()
+                kt.register_kv_cache(big, 36)
+                kt.prewarm_p2p_pairs([(0, 1)], num_layers=36, block_size=256, num_kv_heads=8, head_dim=128,
+                                     num_blocks=2, dtype=torch.bfloat16, timeout_s=20)
+            kt.swap_in(remote_gpu=s_rank, remote_blocks=src_ids, local_gpu=d_rank, kv_cache=big, num_layers=36,
+                       block_size=256, num_kv_heads=8, head_dim=128,
+                       local_target_blocks=dst_ids if rank == d_rank else None, negotiate_blocks=False,
+                       timeout_s=20)
+            dist.barrier()
+            if rank == d_rank:
+                src_cpu = kvgen.seeded_cache(big_shape, s_rank)
+                c_oracle.swap_planned(src_cpu, src_ids, big_cpu, dst_ids, nthreads=8)
+                ok &= _same_bits(big, big_cpu)
+            else:
+                ok &= _same_bits(big, big_cpu)   # the source is unchanged
+        kt.shutdown()
+        dist.barrier()
+        queue.put({"rank": rank, "ok": bool(ok), "obs": obs})
+        dist.destroy_process_group()
+    except Exception as exc:  # noqa: BLE001 - report to the parent
+        queue.put({"rank": rank, "ok": False, "error": repr(exc)})
+        raise
+
+
+@pytest.mark.skipif(device_count() < 2, reason="needs 2 GPUs")
+def test_two_processes_public_api_swap_in(require_gpu):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_swap_worker, args=(r, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    deadline = time.time() + 300
+    try:
+        while len(results) < 2 and time.time() < deadline:
+            try:
+                results.append(queue.get(timeout=1))
+            except Exception:  # noqa: BLE001 - queue.Empty
+                if any(p.exitcode not in (None, 0) for p in procs):
+                    break
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+    assert len(results) == 2, results
+    assert all(r["ok"] for r in results), results
+    obs = next(r["obs"] for r in results if r["rank"] == 0)
+    assert len(obs) == 1 and obs[0]["src_gpu"] == 0 and obs[0]["dst_gpu"] == 1
+    assert obs[0]["transfer_bytes"] == 4 * 2 * 2 * 2 * 1 * 8 * 4
