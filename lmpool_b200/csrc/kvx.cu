@@ -505,18 +505,21 @@ struct LaunchPlan {
     size_t smem;
 };
 
+constexpr size_t kBulkMaxSmem = 227 * 1024;
+
+// Opt in once per device to the largest ring any launch may use; each
+// launch then passes its own (smaller or equal) dynamic shared memory size.
 template <int S>
-int set_bulk_attr(int dev, int idx, size_t smem) {
+int set_bulk_attr(int dev, int idx) {
+    std::lock_guard<std::mutex> lk(g_mu);
     if (!g_bulk_attr_set[dev][idx]) {
         KVX_CUDA(cudaFuncSetAttribute(move_bulk_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)),
+                                      static_cast<int>(kBulkMaxSmem)),
                  "set bulk kernel shared memory");
         g_bulk_attr_set[dev][idx] = true;
     }
     return KVX_OK;
 }
-
-constexpr size_t kBulkMaxSmem = 227 * 1024;
 
 int plan_launch(int dev, int vec, int64_t total_tiles_hint, int64_t chunk_bytes, LaunchPlan* lp) {
     kvx_tuning t;
@@ -527,8 +530,10 @@ int plan_launch(int dev, int vec, int64_t total_tiles_hint, int64_t chunk_bytes,
     int sms = 0;
     int rc = sm_count(dev, &sms);
     if (rc) return rc;
+    // Automatic choice: the bulk-copy engine wherever every address term is
+    // 16-byte aligned (measured faster at every block count), else registers.
     int variant = t.variant;
-    if (variant == 0) variant = 1;
+    if (variant == 0) variant = (vec == 16) ? 2 : 1;
     if (variant == 2 && vec < 16) variant = 1;  // bulk copies need 16-byte granules
     lp->variant = variant;
     lp->vec = vec;
@@ -536,7 +541,8 @@ int plan_launch(int dev, int vec, int64_t total_tiles_hint, int64_t chunk_bytes,
         int64_t tile = t.tile_bytes > 0 ? t.tile_bytes : 32 * 1024;
         tile = std::max<int64_t>(vec, tile / vec * vec);
         lp->tile_bytes = std::min<int64_t>(tile, chunk_bytes);
-        const int cps = t.ctas_per_sm > 0 ? t.ctas_per_sm : 8;
+        // 64 registers x 256 threads: 4 CTAs fill an SM's register file.
+        const int cps = t.ctas_per_sm > 0 ? t.ctas_per_sm : 4;
         lp->grid = sms * cps;
         lp->stages = 0;
         lp->smem = 0;
@@ -572,19 +578,19 @@ int launch_move(int dev, MoveParams& p, const LaunchPlan& lp, cudaStream_t strea
         int rc = KVX_OK;
         switch (lp.stages) {
             case 4:
-                rc = set_bulk_attr<4>(dev, 0, lp.smem);
+                rc = set_bulk_attr<4>(dev, 0);
                 if (!rc) move_bulk_kernel<4><<<grid, 32, lp.smem, stream>>>(p);
                 break;
             case 8:
-                rc = set_bulk_attr<8>(dev, 2, lp.smem);
+                rc = set_bulk_attr<8>(dev, 2);
                 if (!rc) move_bulk_kernel<8><<<grid, 32, lp.smem, stream>>>(p);
                 break;
             case 12:
-                rc = set_bulk_attr<12>(dev, 3, lp.smem);
+                rc = set_bulk_attr<12>(dev, 3);
                 if (!rc) move_bulk_kernel<12><<<grid, 32, lp.smem, stream>>>(p);
                 break;
             default:
-                rc = set_bulk_attr<6>(dev, 1, lp.smem);
+                rc = set_bulk_attr<6>(dev, 1);
                 if (!rc) move_bulk_kernel<6><<<grid, 32, lp.smem, stream>>>(p);
                 break;
         }

@@ -196,8 +196,13 @@ def test_full_config2_size_properties(variant):
     src_ids, dst_ids = perm[:512], perm[512:1024]
 
     def block_sums(t):
-        # per (plane, layer, block) sum of the bf16 bit patterns, accumulated in int64
-        return t.view(torch.int16).view(2, 28, 2048, -1).sum(dim=-1, dtype=torch.int64)
+        # per (plane, layer, block) sum of the bf16 bit patterns, accumulated
+        # in int64 one (plane, layer) slice at a time (bounded temporaries)
+        out = torch.empty(2, 28, 2048, dtype=torch.int64, device=DEV)
+        for kv in range(2):
+            for layer in range(28):
+                out[kv, layer] = t[kv, layer].view(torch.int16).view(2048, -1).sum(dim=-1, dtype=torch.int64)
+        return out
 
     before = block_sums(cache)
     kt.move_blocks(cache, 28, src_ids, dst_ids, synchronize=True)
