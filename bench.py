@@ -185,7 +185,11 @@ def bench_local(args) -> dict:
     from lmpool_b200 import kv_transfer as kt
     from lmpool_b200.layout import affine_layout
 
-    g = LOCAL
+    g = dict(LOCAL)
+    g["N"] = args.cache_blocks or g["N"]
+    g["B"] = args.blocks or g["B"]
+    if 2 * g["B"] > g["N"]:
+        raise SystemExit("--blocks must be at most half of --cache-blocks (source and destination are disjoint)")
     dev_idx = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(dev_idx)
     dev = torch.device("cuda", dev_idx)
@@ -232,6 +236,10 @@ def bench_local(args) -> dict:
     peak, peak_src = hbm_peak()
     achieved = 2 * P / (ms * 1e-3) / 1e9
     traffic = profile_traffic("move_local_config2")
+    if args.quick:
+        print(json.dumps({"quick": True, "blocks": B, "cache_blocks": g["N"], "ms_per_step": ms, "GB/s": value,
+                          "hbm_GB/s": achieved, "frac": achieved / peak}), flush=True)
+        return None
 
     # B sweep, L2 flushed before each timed launch
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -427,6 +435,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--variant", choices=["auto", "register", "bulk"], default="auto")
+    ap.add_argument("--cache-blocks", type=int, default=0,
+                    help="1-GPU cache size in blocks (default: config 2's 2048); for small profiling cases")
+    ap.add_argument("--blocks", type=int, default=0, help="1-GPU blocks moved per step (default 512)")
+    ap.add_argument("--quick", action="store_true",
+                    help="1 GPU: time the headline loop only (no sweep, e2e or CPU baseline); for profiling")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
