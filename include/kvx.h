@@ -174,6 +174,36 @@ int kvx_pair_wait_armed(int32_t device, const kvx_mailbox* my_mailbox, const kvx
 int kvx_pair_push(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* my_mailbox, int32_t my_rank,
                   const kvx_push_target* targets, int32_t num_targets, int32_t* status_dev, void* stream);
 
+/* ---- allocation-free push ---------------------------------------------------
+ * No counterpart in the reference: LMPool has no such entry point.
+ *
+ * Some callers cannot call cudaMalloc: a serving process whose memory is
+ * already handed out (LMPool sizes its KV cache to take the configured share
+ * of all free GPU memory), code that runs while a CUDA graph is being
+ * captured, or a host whose own allocator owns every byte of device memory.
+ * kvx_pair_push keeps its scratch -- one CTA-completion counter per
+ * destination rank -- in the mailbox region, which kvx_mailbox_create
+ * allocates with cudaMalloc. This variant moves the same bytes with the same
+ * kernel, results identical to kvx_pair_push, but keeps those counters in a
+ * fixed array inside this library (KVX_NOALLOC_MAX_PEERS counters, 256
+ * bytes, held by every GPU that loads the library until the process exits),
+ * so it allocates nothing and needs no scratch from the caller. The caller
+ * still passes its inputs and outputs (caches, source ids, and a mailbox
+ * placed in memory it owns: any zeroed region of kvx_mailbox_bytes() bytes).
+ *   - Destination ranks must be < KVX_NOALLOC_MAX_PEERS; larger ranks are
+ *     rejected with KVX_EINVAL.
+ *   - The first call on a device resolves the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call shares the array. Each call clears its destinations'
+ *     counters on `stream` before launching, so calls that overlap on the GPU
+ *     (two streams pushing to the same destination rank at once) race and
+ *     must not be issued.
+ */
+#define KVX_NOALLOC_MAX_PEERS 64
+int kvx_pair_push_noalloc(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* my_mailbox,
+                          int32_t my_rank, const kvx_push_target* targets, int32_t num_targets,
+                          int32_t* status_dev, void* stream);
+
 /* ---- mailbox and CUDA IPC (replaces pair communicators) -------------------
  * kvx_mailbox_create allocates and zeroes a mailbox on `device`
  * (kv_transfer.py:64-71 created a pair NCCL group instead). */

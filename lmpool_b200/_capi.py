@@ -25,6 +25,7 @@ KVX_ETIMEDOUT = 3
 KVX_EPEER = 4
 KVX_ECUDA = 5
 KVX_EUNSUPPORTED = 6
+NOALLOC_MAX_PEERS = 64
 
 DEV_BAD_SRC_ID = 0x01
 DEV_BAD_DST_ID = 0x02
@@ -128,6 +129,7 @@ SIGNATURES: dict[str, tuple] = {
     "kvx_pair_wait_done": (_i32, [_i32, _P(Mailbox), _i32, _u64, _u64, _vp, _vp]),
     "kvx_pair_wait_armed": (_i32, [_i32, _P(Mailbox), _P(Mailbox), _i32, _i32, _i64, _u64, _vp, _vp]),
     "kvx_pair_push": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PushTarget), _i32, _vp, _vp]),
+    "kvx_pair_push_noalloc": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PushTarget), _i32, _vp, _vp]),
     "kvx_mailbox_bytes": (_i32, [_i32, _i64, _P(_u64)]),
     "kvx_mailbox_create": (_i32, [_i32, _i32, _i64, _P(Mailbox)]),
     "kvx_mailbox_destroy": (_i32, [_i32, _P(Mailbox)]),

@@ -993,6 +993,131 @@ int kvx_pair_push(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* 
     return launch_move(device, p, run, static_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free push
+// ---------------------------------------------------------------------------
+// The push kernel's only scratch memory is one CTA-completion counter per
+// destination rank. kvx_pair_push keeps it in the mailbox region (made by
+// kvx_mailbox_create with cudaMalloc); kvx_pair_push_noalloc keeps it here,
+// in file-scope device storage: KVX_NOALLOC_MAX_PEERS * 4 = 256 bytes that
+// every GPU loading this library holds until the process exits. In host
+// code the array's name is only a host-side stand-in; its device address is
+// resolved per device with cudaGetSymbolAddress and passed to the kernel.
+namespace kvx {
+
+static __device__ __align__(256) unsigned int g_noalloc_counters[KVX_NOALLOC_MAX_PEERS];
+static unsigned int* g_noalloc_counters_dev[kMaxDevices] = {};
+
+// Device address of g_noalloc_counters on `dev` (which must be current),
+// resolved on the first call per device.
+static int noalloc_counters(int dev, unsigned int** out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_noalloc_counters_dev[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_counters);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_counters)");
+        }
+        g_noalloc_counters_dev[dev] = static_cast<unsigned int*>(p);
+    }
+    *out = g_noalloc_counters_dev[dev];
+    return KVX_OK;
+}
+
+}  // namespace kvx
+
+extern "C" {
+
+int kvx_pair_push_noalloc(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* my_mb, int32_t my_rank,
+                          const kvx_push_target* targets, int32_t num_targets, int32_t* status_dev, void* stream) {
+    int rc = check_desc(src, "src");
+    if (rc) return rc;
+    rc = check_mailbox(my_mb, "local");
+    if (rc) return rc;
+    if (targets == nullptr || num_targets <= 0 || num_targets > kMaxSegments)
+        return fail(KVX_EINVAL, "num_targets must be in [1, %d]", kMaxSegments);
+    if (status_dev == nullptr) return fail(KVX_EINVAL, "status_dev is NULL");
+    if (device < 0 || device >= kMaxDevices) return fail(KVX_EINVAL, "device %d out of range", device);
+    std::vector<const kvx_cache_desc*> others;
+    std::unordered_set<int> ranks;
+    for (int s = 0; s < num_targets; ++s) {
+        const kvx_push_target& t = targets[s];
+        if (t.dst_rank < 0 || t.dst_rank >= KVX_NOALLOC_MAX_PEERS)
+            return fail(KVX_EINVAL,
+                        "target %d: destination rank %d is beyond the %d ranks the allocation-free push "
+                        "supports (its scratch is a fixed array); use kvx_pair_push",
+                        s, t.dst_rank, KVX_NOALLOC_MAX_PEERS);
+        rc = check_desc(&t.dst, "target dst");
+        if (rc) return rc;
+        rc = check_mailbox(&t.dst_mailbox, "target");
+        if (rc) return rc;
+        if (t.dst.num_layers != src->num_layers || t.dst.chunk_bytes != src->chunk_bytes)
+            return fail(KVX_EINVAL, "target %d geometry differs from the source cache", s);
+        if (t.num_ids < 0 || t.num_ids > my_mb->max_blocks)
+            return fail(KVX_EINVAL, "target %d: %lld ids exceed mailbox capacity", s, (long long)t.num_ids);
+        if (t.num_ids > 0 && t.src_ids_dev == nullptr) return fail(KVX_EINVAL, "target %d: src ids NULL", s);
+        if (t.dst_rank >= my_mb->max_peers || t.dst_rank == my_rank)
+            return fail(KVX_EINVAL, "target %d: bad dst_rank %d", s, t.dst_rank);
+        if (my_rank < 0 || my_rank >= t.dst_mailbox.max_peers) return fail(KVX_EINVAL, "my_rank out of range");
+        if (!ranks.insert(t.dst_rank).second) return fail(KVX_EINVAL, "target rank %d listed twice", t.dst_rank);
+        others.push_back(&t.dst);
+    }
+    KVX_DEVICE_GUARD(device);
+    unsigned int* counters = nullptr;
+    rc = noalloc_counters(device, &counters);
+    if (rc) return rc;
+    const int vec = pick_vec(src, others);
+    LaunchPlan lp;
+    rc = plan_launch(device, vec, 0, src->chunk_bytes, &lp);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The array keeps whatever the last call left; this launch's counters
+    // must start at zero (stream-ordered, no allocation).
+    for (int s = 0; s < num_targets; ++s)
+        KVX_CUDA(cudaMemsetAsync(counters + targets[s].dst_rank, 0, sizeof(unsigned int), st),
+                 "clear push counters");
+
+    const MailboxLayout m = mailbox_layout(my_mb->max_peers, my_mb->max_blocks);
+    MoveParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.src_base = src->base;
+    p.src_kv_stride = src->kv_stride;
+    p.src_layer_stride = src->layer_stride;
+    p.src_block_stride = src->block_stride;
+    p.src_num_blocks = src->num_blocks;
+    p.chunk_bytes = src->chunk_bytes;
+    p.tile_bytes = lp.tile_bytes;
+    p.tiles_per_chunk = (src->chunk_bytes + lp.tile_bytes - 1) / lp.tile_bytes;
+    p.num_layers = src->num_layers;
+    p.num_segs = num_targets;
+    p.status = status_dev;
+    for (int s = 0; s < num_targets; ++s) {
+        const kvx_push_target& t = targets[s];
+        const MailboxLayout md = mailbox_layout(t.dst_mailbox.max_peers, t.dst_mailbox.max_blocks);
+        SegParams& g = p.seg[s];
+        g.dst_base = t.dst.base;
+        g.dst_kv_stride = t.dst.kv_stride;
+        g.dst_layer_stride = t.dst.layer_stride;
+        g.dst_block_stride = t.dst.block_stride;
+        g.dst_num_blocks = t.dst.num_blocks;
+        g.src_ids = t.src_ids_dev;
+        g.dst_ids = mb_ptr<int64_t>(my_mb, m.ids, static_cast<int64_t>(t.dst_rank) * my_mb->max_blocks);
+        g.num_ids = t.num_ids;
+        g.num_tiles = t.num_ids * 2 * static_cast<int64_t>(src->num_layers) * p.tiles_per_chunk;
+        if (t.num_ids == 0) g.num_ids = 1;
+        g.go = mb_ptr<uint64_t>(my_mb, m.go, t.dst_rank);
+        g.counter = counters + t.dst_rank;
+        g.flag = mb_ptr<uint64_t>(&t.dst_mailbox, md.done, my_rank);
+    }
+    assign_ctas(p, lp.grid);
+    LaunchPlan run = lp;
+    run.grid = total_ctas(p);
+    return launch_move(device, p, run, st);
+}
+
 int kvx_ipc_export(int32_t device, const void* dev_ptr, void* handle_out_64, uint64_t* offset_out) {
     if (dev_ptr == nullptr || handle_out_64 == nullptr || offset_out == nullptr)
         return fail(KVX_EINVAL, "NULL argument");
