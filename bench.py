@@ -180,6 +180,82 @@ def cpu_reference(g: dict, blocks: int, steps: int, warmup: int, min_seconds: fl
 # 1 GPU: config 2
 # ---------------------------------------------------------------------------
 
+STORE = dict(L=80, H=8, D=128, bs=16, N=4096, T=256)
+
+
+def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30) -> dict:
+    """store_kvcache at BASELINE config 5 geometry (L=80, H=8, D=128,
+    block_size=16, T=256 tokens per step, ~10% padding slots; the cache is
+    shrunk to 4096 blocks: the cost does not depend on N). A step writes every
+    layer: 80 single-layer launches as the model issues them (eager, and
+    captured in a CUDA graph as the decode path does), or one all-layer
+    launch. L2 is flushed between timed steps."""
+    from lmpool_b200.attention import store_kvcache, store_kvcache_layers
+    from lmpool_b200.kv_transfer import check_device_status
+
+    c = STORE
+    dev = torch.device("cuda", dev_idx)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    cache = torch.empty((2, c["L"], c["N"], c["bs"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev)
+    cache.normal_(generator=gen)
+    keys = torch.empty((c["L"], c["T"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    values = torch.empty_like(keys).normal_(generator=gen)
+    g = torch.Generator().manual_seed(55)
+    slots = torch.randperm(c["N"] * c["bs"], generator=g)[:c["T"]].to(torch.int64)
+    slots[torch.rand(c["T"], generator=g) < 0.1] = -1
+    valid = int((slots >= 0).sum())
+    slots = slots.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def per_layer():
+        for layer in range(c["L"]):
+            store_kvcache(keys[layer], values[layer], cache[0, layer], cache[1, layer], slots, c["bs"])
+
+    def all_layers():
+        store_kvcache_layers(keys, values, cache, slots, c["bs"])
+
+    per_layer()
+    all_layers()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        per_layer()
+    torch.cuda.synchronize()
+
+    def timed(fn) -> float:
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return statistics.median(times)
+
+    ms_eager = timed(per_layer)
+    ms_graph = timed(graph.replay)
+    ms_all = timed(all_layers)
+    check_device_status(dev_idx)
+    row = c["H"] * c["D"] * 2
+    traffic = c["L"] * (2 * c["T"] * row + 2 * valid * row + c["T"] * 8)
+    del graph, cache, keys, values, flush
+    torch.cuda.empty_cache()
+
+    def entry(ms, launches):
+        gbs = traffic / (ms * 1e-3) / 1e9
+        return {"ms_per_step": ms, "launches_per_step": launches, "GB/s": gbs, "frac_hbm": gbs / peak}
+
+    return {"geometry": dict(c, valid_tokens=valid), "bytes_per_step": traffic,
+            "per_layer_eager": entry(ms_eager, c["L"]), "per_layer_graph": entry(ms_graph, c["L"]),
+            "all_layers_one_launch": entry(ms_all, 1),
+            "note": "bytes = per layer: read K,V rows of all T tokens + write K,V rows of valid tokens + slot ids"}
+
+
 def bench_local(args) -> dict:
     from lmpool_b200 import _capi
     from lmpool_b200 import kv_transfer as kt
@@ -282,6 +358,7 @@ def bench_local(args) -> dict:
     _capi.lib().kvx_get_tuning(_capi.ctypes.byref(tune))
     del cache
     torch.cuda.empty_cache()
+    store = bench_store_kvcache(dev_idx, peak)
     cpu = cpu_reference(g, CPU_SAMPLE_BLOCKS, steps=3, warmup=1, min_seconds=10.0)
     return {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -302,6 +379,7 @@ def bench_local(args) -> dict:
         "gpu_launches": args.steps,
         "clocks": clk,
         "sweep": sweep,
+        "store_kvcache": store,
         "kernel": {"variant": {0: "auto", 1: "register", 2: "bulk"}[tune.variant], "launches_per_step": 1},
     }
 
@@ -309,6 +387,133 @@ def bench_local(args) -> dict:
 # ---------------------------------------------------------------------------
 # N GPUs: config 4 phase A
 # ---------------------------------------------------------------------------
+
+def block_sums(cache: torch.Tensor, ids: list[int]) -> torch.Tensor:
+    """Per (plane, layer, block) sum of the bf16 bit patterns of the listed
+    blocks, int64, one (plane, layer) slice at a time (bounded temporaries)."""
+    idx = torch.tensor(ids, dtype=torch.int64, device=cache.device)
+    out = torch.empty(2, cache.shape[1], len(ids), dtype=torch.int64, device=cache.device)
+    for kv in range(2):
+        for layer in range(cache.shape[1]):
+            sel = cache[kv, layer].index_select(0, idx).view(torch.int16).reshape(len(ids), -1)
+            out[kv, layer] = sel.sum(-1, dtype=torch.int64)
+    return out.cpu()
+
+
+def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
+    """BASELINE config 3 on ranks 0 -> 1: B in {1, 8, 64, 256}, contiguous and
+    scattered source ids. Each timed run is K back-to-back transfers (publish
+    -> wait_armed -> push -> wait_done), cycling through disjoint id sets so
+    no transfer re-reads blocks still in L2; time = max over the two ranks."""
+    dev = torch.device("cuda", ep.device)
+    N = g["N"]
+    out = []
+    for B in (1, 8, 64, 256):
+        for mode in ("contiguous", "scattered"):
+            K = 20 if B <= 64 else 8
+            nsets = max(1, min(K, (N // 2) // B))
+            gen = torch.Generator().manual_seed(3000 + B)
+            if mode == "contiguous":
+                starts = torch.randint(0, N - B, (nsets,), generator=gen).tolist()
+                src_sets = [list(range(st, st + B)) for st in starts]
+            else:
+                perm = seeded_perm(N, 3100 + B)
+                src_sets = [perm[i * B:(i + 1) * B] for i in range(nsets)]
+            dperm = seeded_perm(N, 3200 + B)
+            dst_sets = [dperm[i * B:(i + 1) * B] for i in range(nsets)]
+            mine = src_sets if rank == 0 else dst_sets
+            tens = [torch.tensor(x, dtype=torch.int64, device=dev) for x in mine]
+
+            def one(k):
+                if rank == 1:
+                    token = ep.next_token(0)
+                    ep.publish(link, tens[k % nsets], B, token, stream)
+                    ep.wait_done(0, token, 60.0, stream)
+                else:
+                    ep.wait_armed(link, B, 60.0, stream)
+                    ep.push(ep.cache, [(link, link.cache, tens[k % nsets], B)], stream)
+
+            for k in range(3):
+                one(k)
+            torch.cuda.synchronize()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for k in range(K):
+                one(k)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) / K], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            pb = payload_bytes(g, B)
+            out.append({"blocks": B, "ids": mode, "bytes": pb, "ms": ms, "GB/s": pb / (ms * 1e-3) / 1e9,
+                        "frac_nvlink": pb / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS})
+    return out
+
+
+def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist) -> dict:
+    """BASELINE config 4 phase B: every rank sends B=32 seeded-random blocks to
+    every other rank at once, into disjoint reserved sets; one push launch per
+    rank carries all its destinations."""
+    dev = torch.device("cuda", ep.device)
+    N, B = g["N"], 32
+    peers = [r for r in range(world) if r != rank]
+    perm = seeded_perm(N, 5000 + rank)
+    incoming = {s: perm[i * B:(i + 1) * B] for i, s in enumerate(peers)}
+    pool = perm[B * len(peers):]
+    outgoing = {}
+    for d in peers:
+        sel = seeded_perm(len(pool), 6000 + 16 * rank + d)[:B]
+        outgoing[d] = [pool[i] for i in sel]
+    links = {r: ep.get_link(r) for r in peers}
+    in_t = {s: torch.tensor(v, dtype=torch.int64, device=dev) for s, v in incoming.items()}
+    out_t = {d: torch.tensor(v, dtype=torch.int64, device=dev) for d, v in outgoing.items()}
+
+    def step():
+        tokens = {}
+        for s in peers:
+            tokens[s] = ep.next_token(s)
+            ep.publish(links[s], in_t[s], B, tokens[s], stream)
+        for d in peers:
+            ep.wait_armed(links[d], B, 60.0, stream)
+        ep.push(ep.cache, [(links[d], links[d].cache, out_t[d], B) for d in peers], stream)
+        for s in peers:
+            ep.wait_done(s, tokens[s], 60.0, stream)
+
+    ep.status.zero_()
+    for _ in range(3):
+        step()
+    K = 10
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / K], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    mine = {"rank": rank, "bits": int(ep.status.item()),
+            "out": {d: block_sums(cache, v) for d, v in outgoing.items()},
+            "in": {s: block_sums(cache, v) for s, v in incoming.items()}}
+    gathered: list = [None] * world
+    dist.all_gather_object(gathered, mine)
+    ok = all(x["bits"] == 0 for x in gathered)
+    for x in gathered:
+        for d, sums in x["out"].items():
+            ok &= torch.equal(sums, gathered[d]["in"][x["rank"]])
+    pb = payload_bytes(g, B)
+    per_gpu_out = (world - 1) * pb / (ms * 1e-3) / 1e9
+    return {"ok": bool(ok), "blocks_per_destination": B, "ms_per_step": ms,
+            "value": world * (world - 1) * pb / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "per_gpu_egress_GB/s": per_gpu_out, "frac_nvlink_per_gpu_egress": per_gpu_out / NVLINK_PEER_GBS,
+            "verified": bool(ok)}
+
 
 def bench_pairs(args) -> dict | None:
     import torch.distributed as dist
@@ -375,12 +580,16 @@ def bench_pairs(args) -> dict | None:
     ms = float(t.item())
     bits = int(ep.status.item())
     # correctness: checksums of what this rank sent vs what its partner holds
-    sums_src = cache[:, :, src_ids].view(torch.int16).reshape(2, g["L"], B, -1).sum(-1, dtype=torch.int64).cpu()
-    sums_dst = cache[:, :, dst_ids].view(torch.int16).reshape(2, g["L"], B, -1).sum(-1, dtype=torch.int64).cpu()
+    sums_src = block_sums(cache, src_ids)
+    sums_dst = block_sums(cache, dst_ids)
     gathered: list = [None] * world
     dist.all_gather_object(gathered, {"rank": rank, "src": sums_src, "dst": sums_dst, "bits": bits, "clk": clk})
     ok = all(item["bits"] == 0 for item in gathered)
     ok &= torch.equal(gathered[partner]["src"], sums_dst)
+
+    sweep = pair_sweep(ep, link, g, rank, stream, dist) if world == 2 else None
+    phase_b = all_partner(ep, cache, g, rank, world, stream, dist) if world >= 4 else None
+    ok &= phase_b is None or phase_b["ok"]
 
     # end to end: host id lists through swap_batch (pinned H2D + status D2H per step)
     e2e_steps = max(3, min(args.steps, 30))
@@ -425,6 +634,8 @@ def bench_pairs(args) -> dict | None:
                 "api": "lmpool_b200.kv_transfer.swap_batch(host id lists)"},
         "gpu_launches": 4 * args.steps,
         "clocks": merge_clocks([item["clk"] for item in gathered]),
+        "pair_sweep": sweep,
+        "phase_b": ({k: v for k, v in phase_b.items() if k != "ok"} if phase_b else None),
     }
 
 

@@ -30,9 +30,11 @@ from __future__ import annotations
 import logging
 import os
 import socket
+import threading
 import time
 from typing import Iterable, List, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -125,19 +127,87 @@ def check_device_status(device: int | None = None, reset: bool = True) -> int:
     return bits
 
 
-def _ids_tensor(ids: List[int], device: int) -> torch.Tensor:
-    host = torch.tensor([int(b) for b in ids], dtype=torch.int64)
-    if len(ids) == 0:
-        return host.to(torch.device("cuda", device))
-    return host.pin_memory().to(torch.device("cuda", device), non_blocking=True)
+def _id_array(ids) -> np.ndarray:
+    """Block ids as a contiguous int64 numpy array (lists, tuples, arrays, CPU tensors)."""
+    if isinstance(ids, torch.Tensor):
+        return np.ascontiguousarray(ids.detach().cpu().numpy().astype(np.int64, copy=False))
+    return np.ascontiguousarray(np.asarray(ids, dtype=np.int64).reshape(-1))
 
 
-def _validate(ids: List[int], num_blocks: int, distinct: bool, what: str) -> None:
-    lib = _capi.lib()
-    arr = (_capi.ctypes.c_int64 * max(1, len(ids)))(*[int(b) for b in ids])
-    rc = lib.kvx_validate_block_ids(arr, len(ids), int(num_blocks), 1 if distinct else 0)
+class _IdStager:
+    """Host -> device staging of block ids for one device.
+
+    Ids of a call are packed into one reusable pinned buffer and copied to a
+    fresh device tensor with a single asynchronous copy on the caller's
+    stream. An event recorded after the copy guards the pinned buffer: the
+    next call waits for it (normally long complete) before overwriting.
+    """
+
+    def __init__(self, device: int):
+        self.device = device
+        self.pinned: torch.Tensor | None = None
+        self.host: np.ndarray | None = None
+        self.event: torch.cuda.Event | None = None
+        self.lock = threading.Lock()
+
+    def upload(self, stream, *arrays: np.ndarray) -> list[torch.Tensor]:
+        total = int(sum(a.size for a in arrays))
+        dev = torch.device("cuda", self.device)
+        if total == 0:
+            return [torch.empty(0, dtype=torch.int64, device=dev) for _ in arrays]
+        with self.lock:
+            if self.event is not None:
+                self.event.synchronize()
+            if self.pinned is None or self.pinned.numel() < total:
+                self.pinned = torch.empty(max(total, 4096), dtype=torch.int64).pin_memory()
+                self.host = self.pinned.numpy()
+            off = 0
+            for a in arrays:
+                self.host[off:off + a.size] = a
+                off += a.size
+            with torch.cuda.stream(stream):
+                out = torch.empty(total, dtype=torch.int64, device=dev)
+                out.copy_(self.pinned[:total], non_blocking=True)
+                self.event = torch.cuda.Event()
+                self.event.record(stream)
+        views, off = [], 0
+        for a in arrays:
+            views.append(out[off:off + a.size])
+            off += a.size
+        return views
+
+
+_STAGERS: dict[int, _IdStager] = {}
+
+
+def _upload(device: int, stream, *arrays: np.ndarray) -> list[torch.Tensor]:
+    st = _STAGERS.get(device)
+    if st is None:
+        st = _STAGERS.setdefault(device, _IdStager(device))
+    return st.upload(stream, *arrays)
+
+
+def _ids_tensor(ids, device: int, stream=None) -> torch.Tensor:
+    stream = torch.cuda.current_stream(device) if stream is None else stream
+    return _upload(device, stream, _id_array(ids))[0]
+
+
+def _validate(ids, num_blocks: int, distinct: bool, what: str) -> np.ndarray:
+    """Host check of block ids (range, and distinctness for targets); returns the id array."""
+    arr = _id_array(ids)
+    rc = _capi.lib().kvx_validate_block_ids(arr.ctypes.data if arr.size else None, arr.size, int(num_blocks),
+                                            1 if distinct else 0)
     if rc != _capi.KVX_OK:
         raise RuntimeError(f"{what}: {_capi.last_error()}")
+    return arr
+
+
+def _overlap(a: np.ndarray, b: np.ndarray, num_blocks: int) -> bool:
+    out = _capi.ctypes.c_int32(0)
+    _capi.check(_capi.lib().kvx_ids_overlap(a.ctypes.data if a.size else None, a.size,
+                                            b.ctypes.data if b.size else None, b.size, int(num_blocks),
+                                            _capi.ctypes.byref(out)), "kvx_ids_overlap")
+    return bool(out.value)
 
 
 def _launch_move(device: int, src: CacheLayout, dst: CacheLayout, src_ids: torch.Tensor | None,
@@ -290,21 +360,17 @@ def move_blocks(kv_cache, num_layers: int, src_blocks: List[int], dst_blocks: Li
     device = _require_cuda(first_k, "kv_cache")
     src = cache_layouts(kv_cache, num_layers)
     dst = cache_layouts(dst_kv_cache, num_layers)
-    _validate(src_blocks, src[0].num_blocks, False, "move_blocks source")
-    _validate(dst_blocks, dst[0].num_blocks, True, "move_blocks destination")
+    src_arr = _validate(src_blocks, src[0].num_blocks, False, "move_blocks source")
+    dst_arr = _validate(dst_blocks, dst[0].num_blocks, True, "move_blocks destination")
     stream = torch.cuda.current_stream(device) if stream is None else stream
     same = [s.base for s in src] == [d.base for d in dst]
-    if same:
-        overlap = bool(set(int(b) for b in src_blocks) & set(int(b) for b in dst_blocks))
-    else:
-        overlap = False
+    overlap = same and _overlap(src_arr, dst_arr, src[0].num_blocks)
     with torch.cuda.stream(stream):
         if overlap:
             payload = _pack_all_layer_blocks(kv_cache, num_layers, src_blocks)
             _unpack_all_layer_blocks(payload, dst_kv_cache, dst_blocks)
         else:
-            sid = _ids_tensor(src_blocks, device)
-            did = _ids_tensor(dst_blocks, device)
+            sid, did = _upload(device, stream, src_arr, dst_arr)
             _move_layouts(device, src, dst, sid, did, len(src_blocks), num_layers, stream)
     if synchronize:
         check_device_status(device)

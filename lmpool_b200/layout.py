@@ -143,10 +143,73 @@ def _single_layer(k: torch.Tensor, v: torch.Tensor) -> CacheLayout:
     )
 
 
+def _tensor_layout(t: torch.Tensor, num_layers: int) -> CacheLayout:
+    """Layout of a [2, L, N, ...] (6-D) or [2, N, ...] (5-D, one layer) tensor,
+    read from its strides without building per-layer views."""
+    six = t.dim() == 6
+    if six and num_layers > t.shape[1]:
+        raise IndexError(f"index {t.shape[1]} is out of bounds for dimension 1 with size {t.shape[1]}")
+    inner = t.shape[3:] if six else t.shape[2:]
+    inner_strides = t.stride()[3:] if six else t.stride()[2:]
+    expected = 1
+    for size, stride in reversed(list(zip(inner, inner_strides))):
+        if size != 1 and stride != expected:
+            raise RuntimeError("k_cache: each block [block_size, heads, dim] must be contiguous")
+        expected *= size
+    e = t.element_size()
+    chunk = e
+    for size in inner:
+        chunk *= int(size)
+    return CacheLayout(
+        base=t.data_ptr(),
+        kv_stride=t.stride(0) * e,
+        layer_stride=(t.stride(1) * e) if six else 0,
+        block_stride=(t.stride(2) if six else t.stride(1)) * e,
+        num_blocks=int(t.shape[2] if six else t.shape[1]),
+        chunk_bytes=chunk,
+        num_layers=num_layers,
+        dtype=t.dtype,
+        device=t.device,
+        block_shape=tuple(int(s) for s in inner),
+    )
+
+
+def _list_layouts(kv_cache, num_layers: int) -> list[CacheLayout]:
+    """Per-layer (k, v) pairs, from the existing tensors: the first pair is
+    checked in full, the others against its shape/strides/dtype/device; the
+    result is one affine layout when the pointers sit at a constant stride."""
+    k0, v0 = kv_cache[0][0], kv_cache[0][1]
+    first = _single_layer(k0, v0)
+    sig = (tuple(k0.shape), k0.stride(), k0.dtype, k0.device)
+    kptr = [0] * num_layers
+    vptr = [0] * num_layers
+    uniform = True
+    for layer in range(num_layers):
+        k, v = kv_cache[layer][0], kv_cache[layer][1]
+        if layer and ((tuple(k.shape), k.stride(), k.dtype, k.device) != sig
+                      or (tuple(v.shape), v.stride(), v.dtype, v.device) != sig):
+            uniform = False
+            break
+        kptr[layer] = k.data_ptr()
+        vptr[layer] = v.data_ptr()
+    if uniform:
+        step = kptr[1] - kptr[0] if num_layers > 1 else 0
+        kv = vptr[0] - kptr[0]
+        if all(kptr[i] == kptr[0] + i * step and vptr[i] == kptr[i] + kv for i in range(num_layers)):
+            return [CacheLayout(base=first.base, kv_stride=kv, layer_stride=step, block_stride=first.block_stride,
+                                num_blocks=first.num_blocks, chunk_bytes=first.chunk_bytes, num_layers=num_layers,
+                                dtype=first.dtype, device=first.device, block_shape=first.block_shape)]
+    return [_single_layer(kv_cache[layer][0], kv_cache[layer][1]) for layer in range(num_layers)]
+
+
 def cache_layouts(kv_cache, num_layers: int) -> list[CacheLayout]:
     """One affine layout covering all layers if possible, else one per layer."""
     if num_layers <= 0:
         raise RuntimeError(f"num_layers must be positive, got {num_layers}")
+    if isinstance(kv_cache, torch.Tensor) and kv_cache.dim() in (5, 6):
+        return [_tensor_layout(kv_cache, num_layers)]
+    if isinstance(kv_cache, (list, tuple)) and kv_cache and isinstance(kv_cache[0], (list, tuple)):
+        return _list_layouts(kv_cache, num_layers)
     per_layer = [_single_layer(*get_layer_kv(kv_cache, layer)) for layer in range(num_layers)]
     first = per_layer[0]
     for lay in per_layer[1:]:

@@ -214,29 +214,26 @@ def _swap_worker(rank: int, port: int, queue) -> None:
             ok &= bool((cache[0, :, 2] == 1.0).all() and (cache[1, :, 2] == 1.5).all())
             ok &= bool((cache[0, :, 3] == 2.0).all() and (cache[1, :, 3] == 2.5).all())
             ok &= bool(cache[:, :, [0, 1] + list(range(4, 16))].abs().sum().item() == 0)
-        # seeded bf16 transfer at Qwen3-8B geometry (reduced N), both directions in turn
+        # seeded bf16 transfers at Qwen3-8B geometry (reduced N), both directions
+        # in turn; every rank keeps a CPU model of both caches (the second
+        # transfer may read blocks the first one wrote)
         big_shape = (2, 36, 32, 256, 8, 128)
-        for step, (s_rank, d_rank) in enumerate(((0, 1), (1, 0))):
+        model = [kvgen.seeded_cache(big_shape, r) for r in range(2)]
+        big = model[rank].to(f"cuda:{rank}")
+        kt.shutdown()
+        kt.register_kv_cache(big, 36)
+        kt.prewarm_p2p_pairs([(0, 1)], num_layers=36, block_size=256, num_kv_heads=8, head_dim=128,
+                             num_blocks=2, dtype=torch.bfloat16, timeout_s=20)
+        for step, (s_rank, d_rank) in enumerate(((0, 1), (1, 0), (0, 1))):
             src_ids = kvgen.seeded_perm(32, 100 + step)[:9]
             dst_ids = kvgen.seeded_perm(32, 200 + step)[:9]
-            if step == 0:
-                big_cpu = kvgen.seeded_cache(big_shape, rank)
-                big = big_cpu.to(f"cuda:{rank}")
-                kt.shutdown()
-                kt.register_kv_cache(big, 36)
-                kt.prewarm_p2p_pairs([(0, 1)], num_layers=36, block_size=256, num_kv_heads=8, head_dim=128,
-                                     num_blocks=2, dtype=torch.bfloat16, timeout_s=20)
             kt.swap_in(remote_gpu=s_rank, remote_blocks=src_ids, local_gpu=d_rank, kv_cache=big, num_layers=36,
                        block_size=256, num_kv_heads=8, head_dim=128,
                        local_target_blocks=dst_ids if rank == d_rank else None, negotiate_blocks=False,
                        timeout_s=20)
             dist.barrier()
-            if rank == d_rank:
-                src_cpu = kvgen.seeded_cache(big_shape, s_rank)
-                c_oracle.swap_planned(src_cpu, src_ids, big_cpu, dst_ids, nthreads=8)
-                ok &= _same_bits(big, big_cpu)
-            else:
-                ok &= _same_bits(big, big_cpu)   # the source is unchanged
+            c_oracle.swap_planned(model[s_rank], src_ids, model[d_rank], dst_ids, nthreads=8)
+            ok &= _same_bits(big, model[rank])
         kt.shutdown()
         dist.barrier()
         queue.put({"rank": rank, "ok": bool(ok), "obs": obs})
