@@ -183,7 +183,7 @@ def cpu_reference(g: dict, blocks: int, steps: int, warmup: int, min_seconds: fl
 STORE = dict(L=80, H=8, D=128, bs=16, N=4096, T=256)
 
 
-def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30) -> dict:
+def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: int = 0) -> dict:
     """store_kvcache at BASELINE config 5 geometry (L=80, H=8, D=128,
     block_size=16, T=256 tokens per step, ~10% padding slots; the cache is
     shrunk to 4096 blocks: the cost does not depend on N). A step writes every
@@ -193,7 +193,8 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30) -> dict:
     from lmpool_b200.attention import store_kvcache, store_kvcache_layers
     from lmpool_b200.kv_transfer import check_device_status
 
-    c = STORE
+    c = dict(STORE)
+    c["N"] = num_blocks or c["N"]
     dev = torch.device("cuda", dev_idx)
     gen = torch.Generator(device=dev).manual_seed(5)
     cache = torch.empty((2, c["L"], c["N"], c["bs"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev)
@@ -639,6 +640,216 @@ def bench_pairs(args) -> dict | None:
     }
 
 
+def bench_pair_one_process(args) -> dict:
+    """One process drives cuda:0 (source) and cuda:1 (destination): the pair
+    protocol at Qwen3-8B geometry with launches enqueued in dependency order
+    (publish on 1, wait_armed + push on 0, wait_done on 1), so every bounded
+    wait is satisfied by a launch issued before it. Used for profiling the
+    NVLink push with one process, and as a quick pair number."""
+    from lmpool_b200.endpoint import TransferEndpoint
+    from lmpool_b200.layout import affine_layout
+
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("pair1p needs 2 GPUs")
+    g = dict(PAIRS)
+    g["N"] = args.cache_blocks or g["N"]
+    g["B"] = args.blocks or g["B"]
+    B, N = g["B"], g["N"]
+    if 2 * B > N:
+        raise SystemExit("--blocks must be at most half of --cache-blocks")
+    caches, eps = [], []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        t = torch.empty((2, g["L"], N, g["bs"], g["H"], g["D"]), dtype=torch.bfloat16, device=dev)
+        t.normal_(generator=torch.Generator(device=dev).manual_seed(d))
+        caches.append(t)
+        ep = TransferEndpoint(d, 2, d, N)
+        ep.set_cache(affine_layout(t, g["L"]), t)
+        eps.append(ep)
+    l01 = eps[0].link(eps[1].export_record())
+    l10 = eps[1].link(eps[0].export_record())
+    perm = seeded_perm(N, 11)
+    src_t = torch.tensor(perm[:B], dtype=torch.int64, device="cuda:0")
+    dst_t = torch.tensor(perm[B:2 * B], dtype=torch.int64, device="cuda:1")
+    s0, s1 = torch.cuda.current_stream(0), torch.cuda.current_stream(1)
+
+    def one():
+        token = eps[1].next_token(0)
+        eps[1].publish(l10, dst_t, B, token, s1)
+        eps[0].wait_armed(l01, B, 30.0, s0)
+        eps[0].push(eps[0].cache, [(l01, l01.cache, src_t, B)], s0)
+        eps[1].wait_done(0, token, 30.0, s1)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize(0)
+    torch.cuda.synchronize(1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.device(0):
+        e0.record(s0)
+    for _ in range(args.steps):
+        one()
+    with torch.cuda.device(0):
+        e1.record(s0)
+    torch.cuda.synchronize(0)
+    torch.cuda.synchronize(1)
+    ms = e0.elapsed_time(e1) / args.steps
+    eps[0].check_status(s0, "pair1p source")
+    eps[1].check_status(s1, "pair1p destination")
+    ok = all(torch.equal(caches[1][:, :, perm[B + i]].cpu().view(torch.int16),
+                         caches[0][:, :, perm[i]].cpu().view(torch.int16)) for i in (0, B - 1))
+    for ep in eps:
+        ep.close_links()
+    for ep in eps:
+        ep.close()
+    P = payload_bytes(g, B)
+    return {"workload": "pair, one process, cuda:0 -> cuda:1", "blocks": B, "cache_blocks": N, "ms_per_step": ms,
+            "GB/s": P / (ms * 1e-3) / 1e9, "frac_nvlink": P / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, "verified": ok}
+
+
+CONFIG5 = dict(workload="config5: 70B-like transfer (B=1024 to the NVLink partner, both directions) under "
+                        "concurrent store_kvcache (T=256 tokens x 80 layers per step)",
+               L=80, N=16384, bs=16, H=8, D=128, B=1024, T=256)
+
+
+def bench_config5(args) -> dict | None:
+    """BASELINE config 5 on N GPUs (pairs): the transfer alone, store_kvcache
+    alone, and both at once on two streams. The cache is shrunk from 65536 to
+    16384 blocks per rank (80 GiB; 65536 would be 320 GiB): transfer and store
+    costs depend on B and T, not on N."""
+    import torch.distributed as dist
+
+    from lmpool_b200 import kv_transfer as kt
+    from lmpool_b200.attention import store_kvcache, store_kvcache_layers
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    if world < 2 or world % 2:
+        raise SystemExit("config 5 needs an even number of GPUs >= 2")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    c = CONFIG5
+    cache = torch.empty((2, c["L"], c["N"], c["bs"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    cache.normal_(generator=gen)
+    keys = torch.empty((c["L"], c["T"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    values = torch.empty_like(keys).normal_(generator=gen)
+    kt.register_kv_cache(cache, c["L"])
+    pairs = [(r, r + 1) for r in range(0, world, 2)]
+    kt.prewarm_p2p_pairs(pairs, num_layers=c["L"], block_size=c["bs"], num_kv_heads=c["H"], head_dim=c["D"],
+                         num_blocks=2, dtype=torch.bfloat16, timeout_s=60)
+    partner = rank + 1 if rank % 2 == 0 else rank - 1
+    B = c["B"]
+    perm = seeded_perm(c["N"], 7000 + rank)
+    src_ids, dst_ids = perm[:B], perm[B:2 * B]          # fragmented, disjoint
+    # store_kvcache slots avoid both transfer sets (blocks being moved are
+    # locked: the model never writes them)
+    busy = torch.zeros(c["N"], dtype=torch.bool)
+    busy[src_ids] = True
+    busy[dst_ids] = True
+    free_blocks = (~busy).nonzero().flatten()
+    g = torch.Generator().manual_seed(77 + rank)
+    pick = free_blocks[torch.randperm(len(free_blocks), generator=g)[:c["T"]]]
+    slots = pick * c["bs"] + torch.randint(0, c["bs"], (c["T"],), generator=g)
+    slots[torch.rand(c["T"], generator=g) < 0.1] = -1
+    slots = slots.to(torch.int64).to(dev)
+    ep = kt._ENDPOINTS[local]
+    link = ep.get_link(partner)
+    xs = torch.cuda.Stream(dev)
+    ss = torch.cuda.Stream(dev)
+    src_t = torch.tensor(src_ids, dtype=torch.int64, device=dev)
+    dst_t = torch.tensor(dst_ids, dtype=torch.int64, device=dev)
+    P = B * c["L"] * 2 * c["bs"] * c["H"] * c["D"] * 2
+    row = c["H"] * c["D"] * 2
+    valid = int((slots >= 0).sum())
+    store_bytes = c["L"] * (2 * c["T"] * row + 2 * valid * row + c["T"] * 8)
+
+    def xfer():
+        token = ep.next_token(partner)
+        ep.publish(link, dst_t, B, token, xs)
+        ep.wait_armed(link, B, 60.0, xs)
+        ep.push(ep.cache, [(link, link.cache, src_t, B)], xs)
+        ep.wait_done(partner, token, 60.0, xs)
+
+    def store_step():
+        with torch.cuda.stream(ss):
+            store_kvcache_layers(keys, values, cache, slots, c["bs"])
+
+    with torch.cuda.stream(ss):
+        for layer in range(c["L"]):   # warm the single-layer launch too
+            store_kvcache(keys[layer], values[layer], cache[0, layer], cache[1, layer], slots, c["bs"])
+    ep.status.zero_()
+    for _ in range(3):
+        xfer()
+        store_step()
+    torch.cuda.synchronize()
+
+    def timed_alone(fn, stream, reps) -> float:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    K = max(3, min(args.steps, 10))
+    x_ms = timed_alone(xfer, xs, K)
+    s_ms = timed_alone(store_step, ss, 200)
+    M = max(1, int(K * x_ms / s_ms))
+    # both at once: K transfers on one stream, M store steps on another, same start
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    start.record(torch.cuda.current_stream(dev))
+    xs.wait_event(start)
+    ss.wait_event(start)
+    xe, se = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for k in range(max(K, M)):
+        if k < K:
+            xfer()
+        if k < M:
+            store_step()
+    xe.record(xs)
+    se.record(ss)
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(xe) / K, start.elapsed_time(se) / M], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    xo_ms, so_ms = float(t[0]), float(t[1])
+    bits = int(ep.status.item())
+    oks: list = [None] * world
+    dist.all_gather_object(oks, bits == 0)
+    kt.check_device_status(local)
+    kt.shutdown()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank != 0:
+        return None
+    if not all(oks):
+        raise RuntimeError("config 5 transfer reported a device error")
+    return {
+        "metric": METRIC, "workload": c["workload"], "n_gpus": world, "unit": "GB/s",
+        "config": {k: c[k] for k in ("L", "N", "bs", "H", "D", "B", "T")},
+        "substitution": "num_blocks 65536 -> 16384 per rank (320 GiB does not fit one B200)",
+        "transfer_alone": {"ms": x_ms, "GB/s_per_direction": P / (x_ms * 1e-3) / 1e9,
+                           "frac_nvlink": P / (x_ms * 1e-3) / 1e9 / NVLINK_PEER_GBS},
+        "store_alone": {"ms_per_step": s_ms, "GB/s": store_bytes / (s_ms * 1e-3) / 1e9,
+                        "launch": "all 80 layers in one launch"},
+        "overlapped": {"transfers": K, "store_steps": M, "transfer_ms": xo_ms,
+                       "transfer_GB/s_per_direction": P / (xo_ms * 1e-3) / 1e9,
+                       "store_ms_per_step": so_ms, "store_GB/s": store_bytes / (so_ms * 1e-3) / 1e9},
+        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes,
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -649,6 +860,9 @@ def main() -> None:
     ap.add_argument("--cache-blocks", type=int, default=0,
                     help="1-GPU cache size in blocks (default: config 2's 2048); for small profiling cases")
     ap.add_argument("--blocks", type=int, default=0, help="1-GPU blocks moved per step (default 512)")
+    ap.add_argument("--workload", choices=["default", "config5", "pair1p", "store"], default="default",
+                    help="config5: BASELINE config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
+                         "pair1p: one process, two GPUs, pair push (profiling); store: store_kvcache only")
     ap.add_argument("--quick", action="store_true",
                     help="1 GPU: time the headline loop only (no sweep, e2e or CPU baseline); for profiling")
     args = ap.parse_args()
@@ -678,7 +892,14 @@ def main() -> None:
     if args.variant != "auto":
         t = _capi.Tuning(variant={"register": 1, "bulk": 2}[args.variant])
         _capi.check(_capi.lib().kvx_set_tuning(_capi.ctypes.byref(t)), "kvx_set_tuning")
-    if world > 1 or args.gpus > 1:
+    if args.workload == "config5":
+        res = bench_config5(args)
+    elif args.workload == "pair1p":
+        res = bench_pair_one_process(args)
+    elif args.workload == "store":
+        torch.cuda.set_device(0)
+        res = bench_store_kvcache(0, hbm_peak()[0], num_blocks=args.cache_blocks)
+    elif world > 1 or args.gpus > 1:
         res = bench_pairs(args)
     else:
         res = bench_local(args)

@@ -15,8 +15,6 @@ kernel would write out of bounds for them.
 """
 from __future__ import annotations
 
-import ctypes
-
 import torch
 
 from . import _capi
@@ -26,13 +24,14 @@ from .kv_transfer import _status_word
 def _cache_strides(k_cache: torch.Tensor, v_cache: torch.Tensor) -> tuple[int, int]:
     if k_cache.dim() != 4:
         raise RuntimeError("k_cache must be [num_blocks, block_size, num_kv_heads, head_dim]")
-    if k_cache.stride() != v_cache.stride():
+    st = k_cache.stride()
+    if st != v_cache.stride():
         raise RuntimeError("k_cache and v_cache must have the same strides")
     H, D = k_cache.shape[2], k_cache.shape[3]
-    if k_cache.stride(3) != 1 or (H > 1 and k_cache.stride(2) != D):
+    if st[3] != 1 or (H > 1 and st[2] != D):
         raise RuntimeError("each cache slot [num_kv_heads, head_dim] must be contiguous")
     e = k_cache.element_size()
-    return k_cache.stride(0) * e, k_cache.stride(1) * e
+    return st[0] * e, st[1] * e
 
 
 def _device_of(*tensors: torch.Tensor) -> int:
@@ -43,6 +42,14 @@ def _device_of(*tensors: torch.Tensor) -> int:
         if t.device != dev:
             raise RuntimeError(f"all tensors must be on {dev}, got {t.device}")
     return dev.index if dev.index is not None else torch.cuda.current_device()
+
+
+def _raw_stream(device: int) -> int:
+    """cudaStream_t of the current stream (cheap path; capture streams included)."""
+    try:
+        return torch._C._cuda_getCurrentRawStream(device)
+    except AttributeError:
+        return torch.cuda.current_stream(device).cuda_stream
 
 
 def store_kvcache(
@@ -65,25 +72,22 @@ def store_kvcache(
         raise TypeError(f"slot_mapping must be int64, got {slot_mapping.dtype}")
     if key.dtype != k_cache.dtype or value.dtype != v_cache.dtype:
         raise TypeError("key/value and cache dtypes must match (the copy is bit-exact)")
-    if tuple(k_cache.shape[2:]) != (num_kv_heads, head_dim) or value.shape != key.shape:
+    kshape = k_cache.shape
+    if kshape[2] != num_kv_heads or kshape[3] != head_dim or value.shape != key.shape:
         raise RuntimeError("key/value [T, H, D] must match the cache's [H, D]")
     device = _device_of(key, value, k_cache, v_cache, slot_mapping)
     if num_tokens == 0:
         return
-    slot_mapping = slot_mapping.contiguous()
+    if not slot_mapping.is_contiguous():
+        slot_mapping = slot_mapping.contiguous()
     block_stride, slot_stride = _cache_strides(k_cache, v_cache)
     e = key.element_size()
-    row_bytes = num_kv_heads * head_dim * e
-    status = _status_word(device)
-    stream = torch.cuda.current_stream(device)
-    _capi.check(
-        _capi.lib().kvx_store_kvcache(
-            device, ctypes.c_void_p(key.data_ptr()), ctypes.c_void_p(value.data_ptr()), key.stride(0) * e,
-            value.stride(0) * e, ctypes.c_void_p(k_cache.data_ptr()), ctypes.c_void_p(v_cache.data_ptr()),
-            block_stride, slot_stride, ctypes.c_void_p(slot_mapping.data_ptr()), num_tokens, k_cache.shape[0],
-            int(block_size), row_bytes, ctypes.c_void_p(status.data_ptr()),
-            ctypes.c_void_p(_capi.stream_handle(stream))),
-        "kvx_store_kvcache")
+    rc = _capi.lib().kvx_store_kvcache(
+        device, key.data_ptr(), value.data_ptr(), key.stride(0) * e, value.stride(0) * e, k_cache.data_ptr(),
+        v_cache.data_ptr(), block_stride, slot_stride, slot_mapping.data_ptr(), num_tokens, kshape[0],
+        int(block_size), num_kv_heads * head_dim * e, _status_word(device).data_ptr(), _raw_stream(device))
+    if rc:
+        _capi.check(rc, "kvx_store_kvcache")
 
 
 def store_kvcache_layers(
@@ -122,13 +126,10 @@ def store_kvcache_layers(
     k0, v0 = kv_cache[0, 0], kv_cache[1, 0]
     block_stride, slot_stride = _cache_strides(k0, v0)
     e = keys.element_size()
-    status = _status_word(device)
-    stream = torch.cuda.current_stream(device)
-    _capi.check(
-        _capi.lib().kvx_store_kvcache_layers(
-            device, L, ctypes.c_void_p(keys.data_ptr()), ctypes.c_void_p(values.data_ptr()), keys.stride(0) * e,
-            values.stride(0) * e, keys.stride(1) * e, values.stride(1) * e, ctypes.c_void_p(k0.data_ptr()),
-            ctypes.c_void_p(v0.data_ptr()), kv_cache.stride(1) * e, kv_cache.stride(1) * e, block_stride,
-            slot_stride, ctypes.c_void_p(slot_mapping.data_ptr()), T, kv_cache.shape[2], int(block_size), H * D * e,
-            ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(_capi.stream_handle(stream))),
-        "kvx_store_kvcache_layers")
+    rc = _capi.lib().kvx_store_kvcache_layers(
+        device, L, keys.data_ptr(), values.data_ptr(), keys.stride(0) * e, values.stride(0) * e, keys.stride(1) * e,
+        values.stride(1) * e, k0.data_ptr(), v0.data_ptr(), kv_cache.stride(1) * e, kv_cache.stride(1) * e,
+        block_stride, slot_stride, slot_mapping.data_ptr(), T, kv_cache.shape[2], int(block_size), H * D * e,
+        _status_word(device).data_ptr(), _raw_stream(device))
+    if rc:
+        _capi.check(rc, "kvx_store_kvcache_layers")
