@@ -183,6 +183,41 @@ def cpu_reference(g: dict, blocks: int, steps: int, warmup: int, min_seconds: fl
 STORE = dict(L=80, H=8, D=128, bs=16, N=4096, T=256)
 
 
+def reference_gpu_local(cache: torch.Tensor, L: int, src_ids: list[int], dst_ids: list[int], steps: int) -> dict:
+    """The reference's own GPU algorithm on the same device and data, restated
+    with the same torch ops: _pack_all_layer_blocks (kv_transfer.py:229-248,
+    2*L index_select into a staging payload) then _unpack_all_layer_blocks
+    (:264-276, 2*L index_copy_). Comparison leg, not the product."""
+    dev = cache.device
+    B = len(src_ids)
+    idx_s = torch.tensor(src_ids, dtype=torch.long, device=dev)
+    idx_d = torch.tensor(dst_ids, dtype=torch.long, device=dev)
+
+    def step():
+        payload = torch.empty((L, 2, B, *cache.shape[3:]), dtype=cache.dtype, device=dev)
+        for layer in range(L):
+            torch.index_select(cache[0, layer], 0, idx_s, out=payload[layer, 0])
+            torch.index_select(cache[1, layer], 0, idx_s, out=payload[layer, 1])
+        for layer in range(L):
+            cache[0, layer].index_copy_(0, idx_d, payload[layer, 0])
+            cache[1, layer].index_copy_(0, idx_d, payload[layer, 1])
+
+    for _ in range(2):
+        step()
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    P = B * L * 2 * int(torch.tensor(cache.shape[3:]).prod()) * cache.element_size()
+    return {"algorithm": "torch index_select -> payload -> index_copy_ (kv_transfer.py:229-276), same GPU and data",
+            "launches_per_step": 4 * L, "ms_per_step": ms, "GB/s": P / (ms * 1e-3) / 1e9}
+
+
 def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: int = 0) -> dict:
     """store_kvcache at BASELINE config 5 geometry (L=80, H=8, D=128,
     block_size=16, T=256 tokens per step, ~10% padding slots; the cache is
@@ -355,6 +390,9 @@ def bench_local(args) -> dict:
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
 
+    ref_gpu = reference_gpu_local(cache, g["L"], perm[:B], perm[B:2 * B], steps=max(3, min(args.steps, 20)))
+    ref_gpu["this_kernel_speedup"] = ref_gpu["ms_per_step"] / ms
+
     tune = _capi.Tuning()
     _capi.lib().kvx_get_tuning(_capi.ctypes.byref(tune))
     del cache
@@ -380,6 +418,7 @@ def bench_local(args) -> dict:
         "gpu_launches": args.steps,
         "clocks": clk,
         "sweep": sweep,
+        "reference_gpu_path": ref_gpu,
         "store_kvcache": store,
         "kernel": {"variant": {0: "auto", 1: "register", 2: "bulk"}[tune.variant], "launches_per_step": 1},
     }
@@ -452,6 +491,51 @@ def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
             out.append({"blocks": B, "ids": mode, "bytes": pb, "ms": ms, "GB/s": pb / (ms * 1e-3) / 1e9,
                         "frac_nvlink": pb / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS})
     return out
+
+
+def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, B: int = 64, iters: int = 10) -> dict:
+    """The reference's planned swap_in on the same two GPUs, restated with the
+    same ops (kv_transfer.py:463-470): rank 0 packs with 2*L index_select and
+    NCCL-sends the payload, rank 1 receives it and unpacks with 2*L
+    index_copy_; timed like benchmark_kv_transfer.py:138-170 (barrier,
+    synchronize, wall clock) on the receiving rank. Comparison leg."""
+    dev = cache.device
+    L = g["L"]
+    src_ids = seeded_perm(g["N"], 8000)[:B]
+    dst_ids = seeded_perm(g["N"], 8001)[:B]
+    idx = torch.tensor(src_ids if rank == 0 else dst_ids, dtype=torch.long, device=dev)
+    shape = (L, 2, B, *cache.shape[3:])
+
+    def one():
+        if rank == 0:
+            payload = torch.empty(shape, dtype=cache.dtype, device=dev)
+            for layer in range(L):
+                torch.index_select(cache[0, layer], 0, idx, out=payload[layer, 0])
+                torch.index_select(cache[1, layer], 0, idx, out=payload[layer, 1])
+            dist.send(payload, dst=1)
+        elif rank == 1:
+            payload = torch.empty(shape, dtype=cache.dtype, device=dev)
+            dist.recv(payload, src=0)
+            for layer in range(L):
+                cache[0, layer].index_copy_(0, idx, payload[layer, 0])
+                cache[1, layer].index_copy_(0, idx, payload[layer, 1])
+
+    times = []
+    for k in range(3 + iters):
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        one()
+        torch.cuda.synchronize()
+        if k >= 3:
+            times.append((time.perf_counter() - t0) * 1e3)
+    t = torch.tensor([statistics.mean(times)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    P = payload_bytes(g, B)
+    return {"algorithm": "index_select pack -> NCCL send/recv -> index_copy_ unpack (kv_transfer.py:463-470), "
+                         "wall clock per transfer like benchmark_kv_transfer.py",
+            "blocks": B, "ms": ms, "GB/s": P / (ms * 1e-3) / 1e9}
 
 
 def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist) -> dict:
@@ -589,6 +673,10 @@ def bench_pairs(args) -> dict | None:
     ok &= torch.equal(gathered[partner]["src"], sums_dst)
 
     sweep = pair_sweep(ep, link, g, rank, stream, dist) if world == 2 else None
+    ref_pair = reference_gpu_pair(cache, g, rank, dist) if world == 2 else None
+    if ref_pair is not None and sweep is not None:
+        mine = next(r for r in sweep if r["blocks"] == ref_pair["blocks"] and r["ids"] == "scattered")
+        ref_pair["this_kernel_speedup"] = ref_pair["ms"] / mine["ms"]
     phase_b = all_partner(ep, cache, g, rank, world, stream, dist) if world >= 4 else None
     ok &= phase_b is None or phase_b["ok"]
 
@@ -636,6 +724,7 @@ def bench_pairs(args) -> dict | None:
         "gpu_launches": 4 * args.steps,
         "clocks": merge_clocks([item["clk"] for item in gathered]),
         "pair_sweep": sweep,
+        "reference_gpu_path": ref_pair,
         "phase_b": ({k: v for k, v in phase_b.items() if k != "ok"} if phase_b else None),
     }
 
@@ -646,6 +735,7 @@ def bench_pair_one_process(args) -> dict:
     (publish on 1, wait_armed + push on 0, wait_done on 1), so every bounded
     wait is satisfied by a launch issued before it. Used for profiling the
     NVLink push with one process, and as a quick pair number."""
+    from lmpool_b200 import kv_transfer as kt
     from lmpool_b200.endpoint import TransferEndpoint
     from lmpool_b200.layout import affine_layout
 
@@ -673,7 +763,15 @@ def bench_pair_one_process(args) -> dict:
     dst_t = torch.tensor(perm[B:2 * B], dtype=torch.int64, device="cuda:1")
     s0, s1 = torch.cuda.current_stream(0), torch.cuda.current_stream(1)
 
+    src_on_1 = src_t.to("cuda:1")
+    pull_status = torch.zeros(1, dtype=torch.int32, device="cuda:1")
+
     def one():
+        if args.pull:
+            # destination-driven: cuda:1 bulk-loads the source blocks from
+            # cuda:0's cache over NVLink and stores them locally
+            kt._launch_move(1, l10.cache, eps[1].cache, src_on_1, dst_t, B, pull_status, s1)
+            return
         token = eps[1].next_token(0)
         eps[1].publish(l10, dst_t, B, token, s1)
         eps[0].wait_armed(l01, B, 30.0, s0)
@@ -684,18 +782,21 @@ def bench_pair_one_process(args) -> dict:
         one()
     torch.cuda.synchronize(0)
     torch.cuda.synchronize(1)
+    timed_dev, timed_stream = (1, s1) if args.pull else (0, s0)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.device(0):
-        e0.record(s0)
+    with torch.cuda.device(timed_dev):
+        e0.record(timed_stream)
     for _ in range(args.steps):
         one()
-    with torch.cuda.device(0):
-        e1.record(s0)
+    with torch.cuda.device(timed_dev):
+        e1.record(timed_stream)
     torch.cuda.synchronize(0)
     torch.cuda.synchronize(1)
     ms = e0.elapsed_time(e1) / args.steps
     eps[0].check_status(s0, "pair1p source")
     eps[1].check_status(s1, "pair1p destination")
+    if int(pull_status.item()):
+        raise RuntimeError(f"pull reported status {int(pull_status.item())}")
     ok = all(torch.equal(caches[1][:, :, perm[B + i]].cpu().view(torch.int16),
                          caches[0][:, :, perm[i]].cpu().view(torch.int16)) for i in (0, B - 1))
     for ep in eps:
@@ -703,7 +804,8 @@ def bench_pair_one_process(args) -> dict:
     for ep in eps:
         ep.close()
     P = payload_bytes(g, B)
-    return {"workload": "pair, one process, cuda:0 -> cuda:1", "blocks": B, "cache_blocks": N, "ms_per_step": ms,
+    return {"workload": "pair, one process, cuda:0 -> cuda:1, " + ("pull by cuda:1" if args.pull else "push by cuda:0"),
+            "blocks": B, "cache_blocks": N, "ms_per_step": ms,
             "GB/s": P / (ms * 1e-3) / 1e9, "frac_nvlink": P / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, "verified": ok}
 
 
@@ -863,6 +965,7 @@ def main() -> None:
     ap.add_argument("--workload", choices=["default", "config5", "pair1p", "store"], default="default",
                     help="config5: BASELINE config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
                          "pair1p: one process, two GPUs, pair push (profiling); store: store_kvcache only")
+    ap.add_argument("--pull", action="store_true", help="pair1p: destination pulls instead of source pushing")
     ap.add_argument("--quick", action="store_true",
                     help="1 GPU: time the headline loop only (no sweep, e2e or CPU baseline); for profiling")
     args = ap.parse_args()

@@ -271,3 +271,180 @@ def test_two_processes_public_api_swap_in(require_gpu):
     obs = next(r["obs"] for r in results if r["rank"] == 0)
     assert len(obs) == 1 and obs[0]["src_gpu"] == 0 and obs[0]["dst_gpu"] == 1
     assert obs[0]["transfer_bytes"] == 4 * 2 * 2 * 2 * 1 * 8 * 4
+
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])
+def test_one_push_launch_serves_several_destinations(require_gpu, variant):
+    """Rank 0 pushes to ranks 1, 2 and 3 in ONE launch (one CTA group and one
+    completion counter per destination); all four endpoints share the GPU and
+    every step runs in order on one stream."""
+    lib = require_gpu
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(ctypes.byref(old))
+    lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=variant)))
+    try:
+        shape = (2, 6, 20, 64, 4, 64)
+        N = shape[2]
+        cpus = [kvgen.seeded_cache(shape, 400 + r) for r in range(4)]
+        gpus = [c.to("cuda:0") for c in cpus]
+        eps = [TransferEndpoint(r, 4, 0, N) for r in range(4)]
+        for r in range(4):
+            eps[r].set_cache(affine_layout(gpus[r], shape[1]), gpus[r])
+        recs = [e.export_record() for e in eps]
+        out_links = {d: eps[0].link(recs[d]) for d in (1, 2, 3)}
+        in_links = {d: eps[d].link(recs[0]) for d in (1, 2, 3)}
+        s = torch.cuda.current_stream(0)
+        counts = {1: 5, 2: 0, 3: 9}                      # an empty transfer still completes
+        src_ids = {d: kvgen.seeded_perm(N, 410 + d)[:counts[d]] for d in (1, 2, 3)}
+        dst_ids = {d: kvgen.seeded_perm(N, 420 + d)[:counts[d]] for d in (1, 2, 3)}
+        for e in eps:
+            e.status.zero_()
+        tokens = {}
+        for d in (1, 2, 3):
+            tokens[d] = eps[d].next_token(0)
+            eps[d].publish(in_links[d], _ids(dst_ids[d], 0), counts[d], tokens[d], s)
+        for d in (1, 2, 3):
+            eps[0].wait_armed(out_links[d], counts[d], 5.0, s)
+        eps[0].push(eps[0].cache, [(out_links[d], out_links[d].cache, _ids(src_ids[d], 0), counts[d])
+                                   for d in (1, 2, 3)], s)
+        for d in (1, 2, 3):
+            eps[d].wait_done(0, tokens[d], 5.0, s)
+        for e in eps:
+            e.check_status(s, f"rank {e.rank}")
+        for d in (1, 2, 3):
+            c_oracle.swap_planned(cpus[0], src_ids[d], cpus[d], dst_ids[d], nthreads=4)
+            assert _same_bits(gpus[d], cpus[d]), f"destination {d}"
+        assert _same_bits(gpus[0], cpus[0])
+        for e in eps:
+            e.close_links()
+        for e in eps:
+            e.close()
+    finally:
+        lib.kvx_set_tuning(ctypes.byref(old))
+
+
+class _FakeLayer(torch.nn.Module):
+    pass
+
+
+def _fake_runner(rank: int, cache: torch.Tensor):
+    from lmpool_b200.model_runner import B200KVTransferMixin
+
+    class Runner(B200KVTransferMixin):
+        pass
+
+    r = Runner()
+    r.rank = rank
+    r.block_size = cache.shape[3]
+    r.config = {"num_layers": cache.shape[1], "num_kv_heads": cache.shape[4], "head_dim": cache.shape[5]}
+    r.model = torch.nn.ModuleList([_FakeLayer() for _ in range(cache.shape[1])])
+    for layer, module in enumerate(r.model):
+        module.k_cache = cache[0, layer]
+        module.v_cache = cache[1, layer]
+    return r
+
+
+def _api_worker(rank: int, port: int, queue) -> None:
+    """Rest of the drop-in surface across two processes: ModelRunner mixin,
+    negotiated swap_in, legacy swap_out, swap_batch both ways at once."""
+    import torch.distributed as dist
+
+    from lmpool_b200 import kv_transfer as kt
+
+    try:
+        torch.cuda.set_device(rank)
+        os.environ["LOCAL_RANK"] = str(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", world_size=2, rank=rank)
+        shape = (2, 8, 40, 64, 8, 128)
+        model = [kvgen.seeded_cache(shape, 500 + r) for r in range(2)]
+        cache = model[rank].to(f"cuda:{rank}")
+        runner = _fake_runner(rank, cache)
+        runner.register_kv_cache_for_transfer()
+        kt.prewarm_p2p_pairs([(0, 1)], num_layers=8, block_size=64, num_kv_heads=8, head_dim=128, num_blocks=2,
+                             dtype=torch.bfloat16, timeout_s=20)
+        errors = []
+        chunk = 64 * 8 * 128 * 2
+        if runner.kv_transfer_bytes(3) != 3 * 8 * 2 * chunk:
+            errors.append("kv_transfer_bytes")
+
+        def check(step):
+            dist.barrier()
+            if not _same_bits(cache, model[rank]):
+                errors.append(f"cache differs after {step}")
+
+        # 1. ModelRunner boundary (model_runner.py:747-806)
+        src, dst = kvgen.seeded_perm(40, 510)[:6], kvgen.seeded_perm(40, 511)[:6]
+        if rank == 0:
+            got = runner.execute_swap_out(src, 1)
+            if got != src:
+                errors.append(f"execute_swap_out returned {got}")
+        else:
+            got = runner.execute_swap_in(0, src, local_target_blocks=dst)
+            if got != dst:
+                errors.append(f"execute_swap_in returned {got}")
+        c_oracle.swap_planned(model[0], src, model[1], dst, nthreads=4)
+        check("execute_swap_out/in")
+        # 2. negotiated swap_in (kv_transfer.py:438-452): destination specifies targets
+        src, dst = kvgen.seeded_perm(40, 520)[:4], kvgen.seeded_perm(40, 521)[:4]
+        got = kt.swap_in(remote_gpu=1, remote_blocks=src, local_gpu=0, kv_cache=cache, num_layers=8,
+                         block_size=64, num_kv_heads=8, head_dim=128,
+                         local_target_blocks=dst if rank == 0 else None, negotiate_blocks=True, timeout_s=20)
+        if got != dst:
+            errors.append(f"negotiated swap_in returned {got} on rank {rank}")
+        c_oracle.swap_planned(model[1], src, model[0], dst, nthreads=4)
+        check("negotiated swap_in")
+        # 3. legacy swap_out (kv_transfer.py:310-392): the source names the targets
+        src, dst = kvgen.seeded_perm(40, 530)[:5], kvgen.seeded_perm(40, 531)[:5]
+        got = kt.swap_out(local_gpu=0, blocks_to_evict=src, target_gpu=1, kv_cache=cache, num_layers=8,
+                          block_size=64, num_kv_heads=8, head_dim=128,
+                          target_free_blocks=dst if rank == 0 else None, timeout_s=20)
+        if got != dst:
+            errors.append(f"swap_out returned {got} on rank {rank}")
+        c_oracle.swap_planned(model[0], src, model[1], dst, nthreads=4)
+        check("swap_out")
+        # 4. both directions at once
+        perm = kvgen.seeded_perm(40, 540)
+        out0, out1 = perm[:7], perm[7:14]          # sources on ranks 0 and 1
+        in1, in0 = perm[20:27], perm[27:34]         # targets on ranks 1 and 0 (disjoint from the sources)
+        if rank == 0:
+            kt.swap_batch([(1, out0)], [(0 + 1, in0)], timeout_s=20)
+        else:
+            kt.swap_batch([(0, out1)], [(0, in1)], timeout_s=20)
+        new0, new1 = model[0].clone(), model[1].clone()
+        c_oracle.swap_planned(model[0], out0, new1, in1, nthreads=4)
+        c_oracle.swap_planned(model[1], out1, new0, in0, nthreads=4)
+        model[0], model[1] = new0, new1
+        check("swap_batch")
+        kt.shutdown()
+        queue.put({"rank": rank, "errors": errors})
+        dist.destroy_process_group()
+    except Exception as exc:  # noqa: BLE001
+        queue.put({"rank": rank, "errors": [repr(exc)]})
+        raise
+
+
+@pytest.mark.skipif(device_count() < 2, reason="needs 2 GPUs")
+def test_two_processes_drop_in_api_surface(require_gpu):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_api_worker, args=(r, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    deadline = time.time() + 300
+    try:
+        while len(results) < 2 and time.time() < deadline:
+            try:
+                results.append(queue.get(timeout=1))
+            except Exception:  # noqa: BLE001 - queue.Empty
+                if any(p.exitcode not in (None, 0) for p in procs):
+                    break
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+    assert len(results) == 2, results
+    assert all(not r["errors"] for r in results), results
