@@ -13,8 +13,10 @@ Workloads (synthetic bf16 N(0,1) caches, seeded randperm block ids):
              launch). The B sweep {1,4,16,64,256,512} is reported in "sweep".
   --gpus N>1 BASELINE config 4 phase A: ranks (0,1), (2,3), ... move
              B=128 blocks each way at once at Qwen3-8B geometry (L=36,
-             1536-block cache per rank, 58 GB); a step is one exchange
-             (publish -> wait_armed -> push over NVLink -> wait_done).
+             1536-block cache per rank, 58 GB); a step is one exchange in
+             the transfer mode of lmpool_b200.kv_transfer (default pull: each
+             rank bulk-loads its partner's blocks over NVLink, then waits for
+             the partner's report; push: arm, push, completion wait).
   --impl reference  the reference algorithm on the host cores (C oracle:
              pack into a payload, then unpack; rank 0 only), same geometry.
 
@@ -442,9 +444,9 @@ def block_sums(cache: torch.Tensor, ids: list[int]) -> torch.Tensor:
 
 def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
     """BASELINE config 3 on ranks 0 -> 1: B in {1, 8, 64, 256}, contiguous and
-    scattered source ids. Each timed run is K back-to-back transfers (publish
-    -> wait_armed -> push -> wait_done), cycling through disjoint id sets so
-    no transfer re-reads blocks still in L2; time = max over the two ranks."""
+    scattered source ids. Each timed run is K back-to-back transfers in the
+    configured mode, cycling through disjoint id sets so no transfer re-reads
+    blocks still in L2; time = max over the two ranks."""
     dev = torch.device("cuda", ep.device)
     N = g["N"]
     out = []
@@ -461,17 +463,14 @@ def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
                 src_sets = [perm[i * B:(i + 1) * B] for i in range(nsets)]
             dperm = seeded_perm(N, 3200 + B)
             dst_sets = [dperm[i * B:(i + 1) * B] for i in range(nsets)]
-            mine = src_sets if rank == 0 else dst_sets
-            tens = [torch.tensor(x, dtype=torch.int64, device=dev) for x in mine]
+            src_t = [torch.tensor(x, dtype=torch.int64, device=dev) for x in src_sets]
+            dst_t = [torch.tensor(x, dtype=torch.int64, device=dev) for x in dst_sets]
 
             def one(k):
                 if rank == 1:
-                    token = ep.next_token(0)
-                    ep.publish(link, tens[k % nsets], B, token, stream)
-                    ep.wait_done(0, token, 60.0, stream)
+                    ep.exchange(ep.mode, ep.cache, [], [(0, src_t[k % nsets], dst_t[k % nsets], B)], 60.0, stream)
                 else:
-                    ep.wait_armed(link, B, 60.0, stream)
-                    ep.push(ep.cache, [(link, link.cache, tens[k % nsets], B)], stream)
+                    ep.exchange(ep.mode, ep.cache, [(1, src_t[k % nsets], B)], [], 60.0, stream)
 
             for k in range(3):
                 one(k)
@@ -544,28 +543,29 @@ def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist) -> dict
     rank carries all its destinations."""
     dev = torch.device("cuda", ep.device)
     N, B = g["N"], 32
+
+    def sets_of(r: int):
+        """(incoming targets by source, outgoing sources by destination) of rank r."""
+        others = [x for x in range(world) if x != r]
+        perm = seeded_perm(N, 5000 + r)
+        inc = {s: perm[i * B:(i + 1) * B] for i, s in enumerate(others)}
+        pool = perm[B * len(others):]
+        out = {}
+        for d in others:
+            sel = seeded_perm(len(pool), 6000 + 16 * r + d)[:B]
+            out[d] = [pool[i] for i in sel]
+        return inc, out
+
     peers = [r for r in range(world) if r != rank]
-    perm = seeded_perm(N, 5000 + rank)
-    incoming = {s: perm[i * B:(i + 1) * B] for i, s in enumerate(peers)}
-    pool = perm[B * len(peers):]
-    outgoing = {}
-    for d in peers:
-        sel = seeded_perm(len(pool), 6000 + 16 * rank + d)[:B]
-        outgoing[d] = [pool[i] for i in sel]
-    links = {r: ep.get_link(r) for r in peers}
+    incoming, outgoing = sets_of(rank)
+    peer_out = {s: sets_of(s)[1][rank] for s in peers}      # what each peer sends to this rank
     in_t = {s: torch.tensor(v, dtype=torch.int64, device=dev) for s, v in incoming.items()}
     out_t = {d: torch.tensor(v, dtype=torch.int64, device=dev) for d, v in outgoing.items()}
+    psrc_t = {s: torch.tensor(v, dtype=torch.int64, device=dev) for s, v in peer_out.items()}
 
     def step():
-        tokens = {}
-        for s in peers:
-            tokens[s] = ep.next_token(s)
-            ep.publish(links[s], in_t[s], B, tokens[s], stream)
-        for d in peers:
-            ep.wait_armed(links[d], B, 60.0, stream)
-        ep.push(ep.cache, [(links[d], links[d].cache, out_t[d], B) for d in peers], stream)
-        for s in peers:
-            ep.wait_done(s, tokens[s], 60.0, stream)
+        ep.exchange(ep.mode, ep.cache, [(d, out_t[d], B) for d in peers],
+                    [(s, psrc_t[s], in_t[s], B) for s in peers], 60.0, stream)
 
     ep.status.zero_()
     for _ in range(3):
@@ -626,23 +626,22 @@ def bench_pairs(args) -> dict | None:
     partner = rank + 1 if rank % 2 == 0 else rank - 1
     B = g["B"]
     src_ids = seeded_perm(g["N"], 1000 + rank)[:B]
+    partner_src = seeded_perm(g["N"], 1000 + partner)[:B]
     # destination ids on this rank for the partner's blocks: distinct from
     # this rank's own outgoing sources
     free = [b for b in seeded_perm(g["N"], 2000 + rank) if b not in set(src_ids)]
     dst_ids = free[:B]
     ep = kt._ENDPOINTS[local]
     link = ep.get_link(partner)
+    mode = ep.mode
     stream = torch.cuda.current_stream(dev)
     src_t = torch.tensor(src_ids, dtype=torch.int64, device=dev)
+    psrc_t = torch.tensor(partner_src, dtype=torch.int64, device=dev)
     dst_t = torch.tensor(dst_ids, dtype=torch.int64, device=dev)
     P = payload_bytes(g, B)
 
     def step():
-        token = ep.next_token(partner)
-        ep.publish(link, dst_t, B, token, stream)
-        ep.wait_armed(link, B, 60.0, stream)
-        ep.push(ep.cache, [(link, link.cache, src_t, B)], stream)
-        ep.wait_done(partner, token, 60.0, stream)
+        ep.exchange(mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, stream)
 
     ep.status.zero_()
     for _ in range(args.warmup):
@@ -683,13 +682,13 @@ def bench_pairs(args) -> dict | None:
     # end to end: host id lists through swap_batch (pinned H2D + status D2H per step)
     e2e_steps = max(3, min(args.steps, 30))
     for _ in range(2):
-        kt.swap_batch([(partner, src_ids)], [(partner, dst_ids)])
+        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)])
     dist.barrier()
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(e2e_steps):
-        kt.swap_batch([(partner, src_ids)], [(partner, dst_ids)])
+        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)])
     e3.record(stream)
     torch.cuda.synchronize()
     t2 = torch.tensor([e2.elapsed_time(e3) / e2e_steps], dtype=torch.float64, device=dev)
@@ -721,7 +720,8 @@ def bench_pairs(args) -> dict | None:
         "e2e": {"value": world * P / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 4,
                 "api": "lmpool_b200.kv_transfer.swap_batch(host id lists)"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": (4 if mode == "push" else 2) * args.steps,
+        "transfer_mode": mode,
         "clocks": merge_clocks([item["clk"] for item in gathered]),
         "pair_sweep": sweep,
         "reference_gpu_path": ref_pair,
@@ -870,12 +870,10 @@ def bench_config5(args) -> dict | None:
     valid = int((slots >= 0).sum())
     store_bytes = c["L"] * (2 * c["T"] * row + 2 * valid * row + c["T"] * 8)
 
+    psrc_t = torch.tensor(seeded_perm(c["N"], 7000 + partner)[:B], dtype=torch.int64, device=dev)
+
     def xfer():
-        token = ep.next_token(partner)
-        ep.publish(link, dst_t, B, token, xs)
-        ep.wait_armed(link, B, 60.0, xs)
-        ep.push(ep.cache, [(link, link.cache, src_t, B)], xs)
-        ep.wait_done(partner, token, 60.0, xs)
+        ep.exchange(ep.mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, xs)
 
     def store_step():
         with torch.cuda.stream(ss):
@@ -948,7 +946,7 @@ def bench_config5(args) -> dict | None:
         "overlapped": {"transfers": K, "store_steps": M, "transfer_ms": xo_ms,
                        "transfer_GB/s_per_direction": P / (xo_ms * 1e-3) / 1e9,
                        "store_ms_per_step": so_ms, "store_GB/s": store_bytes / (so_ms * 1e-3) / 1e9},
-        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes,
+        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes, "transfer_mode": ep.mode,
     }
 
 

@@ -96,6 +96,19 @@ class PushTarget(ctypes.Structure):
     ]
 
 
+class PullSource(ctypes.Structure):
+    _fields_ = [
+        ("src", CacheDesc),
+        ("src_mailbox", Mailbox),
+        ("src_ids_dev", ctypes.c_void_p),
+        ("dst_ids_dev", ctypes.c_void_p),
+        ("num_ids", ctypes.c_int64),
+        ("token", ctypes.c_uint64),
+        ("src_rank", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
+
 class Tuning(ctypes.Structure):
     _fields_ = [
         ("variant", ctypes.c_int32),
@@ -129,6 +142,8 @@ SIGNATURES: dict[str, tuple] = {
     "kvx_pair_wait_done": (_i32, [_i32, _P(Mailbox), _i32, _u64, _u64, _vp, _vp]),
     "kvx_pair_wait_armed": (_i32, [_i32, _P(Mailbox), _P(Mailbox), _i32, _i32, _i64, _u64, _vp, _vp]),
     "kvx_pair_push": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PushTarget), _i32, _vp, _vp]),
+    "kvx_pair_pull": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PullSource), _i32, _vp, _vp]),
+    "kvx_pair_wait_pulled": (_i32, [_i32, _P(Mailbox), _i32, _u64, _vp, _vp]),
     "kvx_pair_push_noalloc": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PushTarget), _i32, _vp, _vp]),
     "kvx_mailbox_bytes": (_i32, [_i32, _i64, _P(_u64)]),
     "kvx_mailbox_create": (_i32, [_i32, _i32, _i64, _P(Mailbox)]),

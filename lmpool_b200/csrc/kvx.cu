@@ -62,7 +62,15 @@ struct SegParams {
     int64_t num_tiles;
     const uint64_t* go;      // nullptr: always run; else run iff *go != 0 and signal *go
     unsigned int* counter;   // CTA completion counter (nullptr: no signal)
-    uint64_t* flag;          // destination completion flag
+    uint64_t* flag;          // completion flag written by the segment's last CTA
+    uint64_t token;          // token to signal when go is nullptr (pull)
+    // Per-segment source (pull: each segment reads another peer's cache);
+    // src_base == 0 means the launch-wide source in MoveParams.
+    uint64_t src_base;
+    int64_t src_kv_stride;
+    int64_t src_layer_stride;
+    int64_t src_block_stride;
+    int64_t src_num_blocks;
     int32_t cta_begin;
     int32_t cta_count;
 };
@@ -105,8 +113,14 @@ __device__ __forceinline__ TileAddr decode_tile(const MoveParams& p, const SegPa
     const int64_t kv = kvl / p.num_layers;
     const int64_t sid = g.src_ids ? ld_id(g.src_ids + i) : i;
     const int64_t did = g.dst_ids ? ld_id(g.dst_ids + i) : i;
+    const bool own_src = g.src_base != 0;
+    const uint64_t src_base = own_src ? g.src_base : p.src_base;
+    const int64_t src_kv = own_src ? g.src_kv_stride : p.src_kv_stride;
+    const int64_t src_layer = own_src ? g.src_layer_stride : p.src_layer_stride;
+    const int64_t src_block = own_src ? g.src_block_stride : p.src_block_stride;
+    const int64_t src_blocks = own_src ? g.src_num_blocks : p.src_num_blocks;
     a.ok = true;
-    if (sid < 0 || sid >= p.src_num_blocks) {
+    if (sid < 0 || sid >= src_blocks) {
         if (report) atomicOr(p.status, KVX_DEV_BAD_SRC_ID);
         a.ok = false;
     }
@@ -116,8 +130,7 @@ __device__ __forceinline__ TileAddr decode_tile(const MoveParams& p, const SegPa
     }
     const int64_t off = j * p.tile_bytes;
     a.len = min(p.tile_bytes, p.chunk_bytes - off);
-    a.src = reinterpret_cast<const char*>(p.src_base + kv * p.src_kv_stride + l * p.src_layer_stride +
-                                          sid * p.src_block_stride + off);
+    a.src = reinterpret_cast<const char*>(src_base + kv * src_kv + l * src_layer + sid * src_block + off);
     a.dst = reinterpret_cast<char*>(g.dst_base + kv * g.dst_kv_stride + l * g.dst_layer_stride +
                                     did * g.dst_block_stride + off);
     return a;
@@ -162,7 +175,7 @@ template <int VEC>
 __global__ void __launch_bounds__(kRegThreads) move_reg_kernel(const __grid_constant__ MoveParams p) {
     const int s = find_segment(p);
     const SegParams& g = p.seg[s];
-    uint64_t token = 1;
+    uint64_t token = g.token ? g.token : 1;
     if (g.go != nullptr) {
         token = ld_relaxed_gpu(g.go);
         if (token == 0) return;  // the arm wait failed: this segment does not run
@@ -188,7 +201,7 @@ __global__ void __launch_bounds__(32) move_bulk_kernel(const __grid_constant__ M
 
     const int s = find_segment(p);
     const SegParams& g = p.seg[s];
-    uint64_t token = 1;
+    uint64_t token = g.token ? g.token : 1;
     if (g.go != nullptr) {
         token = ld_relaxed_gpu(g.go);
         if (token == 0) return;
@@ -261,9 +274,14 @@ __global__ void __launch_bounds__(32) move_bulk_kernel(const __grid_constant__ M
 // ---------------------------------------------------------------------------
 
 struct MailboxLayout {
-    uint64_t arm, done, count, consumed, go, counter, ids, total;
+    uint64_t arm, done, count, consumed, go, pulled, pull_consumed, counter, pull_counter, ids, total;
 };
 
+// Per peer p: arm[p], count[p], ids[p][] (written by destination p, push),
+// done[p] (written by source p, push), consumed[p], go[p] (local, push),
+// pulled[p] (written by destination p after it pulled from this rank),
+// pull_consumed[p] (local), counter[p] / pull_counter[p] (CTA completion
+// counters of this rank's push to p / pull from p).
 __host__ __device__ inline MailboxLayout mailbox_layout(int64_t peers, int64_t max_blocks) {
     MailboxLayout m;
     m.arm = 0;
@@ -271,8 +289,11 @@ __host__ __device__ inline MailboxLayout mailbox_layout(int64_t peers, int64_t m
     m.count = m.done + 8 * peers;
     m.consumed = m.count + 8 * peers;
     m.go = m.consumed + 8 * peers;
-    m.counter = m.go + 8 * peers;
-    m.ids = (m.counter + 4 * peers + 255) / 256 * 256;
+    m.pulled = m.go + 8 * peers;
+    m.pull_consumed = m.pulled + 8 * peers;
+    m.counter = m.pull_consumed + 8 * peers;
+    m.pull_counter = m.counter + 4 * peers;
+    m.ids = (m.pull_counter + 4 * peers + 255) / 256 * 256;
     m.total = m.ids + 8 * peers * max_blocks;
     return m;
 }
@@ -332,6 +353,27 @@ __global__ void wait_done_kernel(const uint64_t* done, uint64_t token, uint64_t 
     for (uint64_t poll = 0; poll < max_polls; ++poll) {
         const uint64_t v = ld_acquire_sys(done);
         if ((v & ~kFailBit) == token) {
+            if (v & kFailBit) atomicOr(status, KVX_DEV_PEER_FAILED);
+            return;
+        }
+        if (global_timer_ns() - t0 > timeout_ns) break;
+        __nanosleep(128);
+    }
+    atomicOr(status, KVX_DEV_TIMEOUT);
+}
+
+// Source (pull mode): wait until the destination reports a pull newer than
+// the last one consumed from it; FAIL bit -> the destination's pull failed.
+__global__ void wait_pulled_kernel(const uint64_t* pulled, uint64_t* consumed, uint64_t timeout_ns, int32_t* status) {
+    if (threadIdx.x != 0) return;
+    const uint64_t last = ld_relaxed_gpu(consumed);
+    const uint64_t t0 = global_timer_ns();
+    const uint64_t max_polls = timeout_ns / 64 + 1000000ull;
+    for (uint64_t poll = 0; poll < max_polls; ++poll) {
+        const uint64_t v = ld_acquire_sys(pulled);
+        if ((v & ~kFailBit) > (last & ~kFailBit)) {
+            *consumed = v;
+            __threadfence();
             if (v & kFailBit) atomicOr(status, KVX_DEV_PEER_FAILED);
             return;
         }
@@ -1127,6 +1169,105 @@ int kvx_pair_push_noalloc(int32_t device, const kvx_cache_desc* src, const kvx_m
     LaunchPlan run = lp;
     run.grid = total_ctas(p);
     return launch_move(device, p, run, st);
+}
+
+int kvx_pair_pull(int32_t device, const kvx_cache_desc* dst, const kvx_mailbox* my_mb, int32_t my_rank,
+                  const kvx_pull_source* sources, int32_t num_sources, int32_t* status_dev, void* stream) {
+    int rc = check_desc(dst, "dst");
+    if (rc) return rc;
+    rc = check_mailbox(my_mb, "local");
+    if (rc) return rc;
+    if (sources == nullptr || num_sources <= 0 || num_sources > kMaxSegments)
+        return fail(KVX_EINVAL, "num_sources must be in [1, %d]", kMaxSegments);
+    if (status_dev == nullptr) return fail(KVX_EINVAL, "status_dev is NULL");
+    if (my_rank < 0 || my_rank >= my_mb->max_peers) return fail(KVX_EINVAL, "my_rank out of range");
+    std::vector<const kvx_cache_desc*> others;
+    std::unordered_set<int> ranks;
+    int64_t total_bytes = 0;
+    for (int s = 0; s < num_sources; ++s) {
+        const kvx_pull_source& src = sources[s];
+        rc = check_desc(&src.src, "source");
+        if (rc) return rc;
+        rc = check_mailbox(&src.src_mailbox, "source");
+        if (rc) return rc;
+        if (src.src.num_layers != dst->num_layers || src.src.chunk_bytes != dst->chunk_bytes)
+            return fail(KVX_EINVAL, "source %d geometry differs from the local cache", s);
+        if (src.num_ids < 0) return fail(KVX_EINVAL, "source %d: negative block count", s);
+        if (src.num_ids > 0 && (src.src_ids_dev == nullptr || src.dst_ids_dev == nullptr))
+            return fail(KVX_EINVAL, "source %d: ids NULL", s);
+        if (src.token == 0 || (src.token & kFailBit)) return fail(KVX_EINVAL, "source %d: token out of range", s);
+        if (src.src_rank < 0 || src.src_rank >= my_mb->max_peers || src.src_rank == my_rank)
+            return fail(KVX_EINVAL, "source %d: bad src_rank %d", s, src.src_rank);
+        if (my_rank >= src.src_mailbox.max_peers) return fail(KVX_EINVAL, "my_rank beyond the source mailbox");
+        if (!ranks.insert(src.src_rank).second) return fail(KVX_EINVAL, "source rank %d listed twice", src.src_rank);
+        others.push_back(&src.src);
+        total_bytes += src.num_ids * 2 * static_cast<int64_t>(dst->num_layers) * dst->chunk_bytes;
+    }
+    KVX_DEVICE_GUARD(device);
+    const int vec = pick_vec(dst, others);
+    LaunchPlan lp;
+    rc = plan_launch(device, vec, total_bytes, dst->chunk_bytes, &lp);
+    if (rc) return rc;
+
+    const MailboxLayout m = mailbox_layout(my_mb->max_peers, my_mb->max_blocks);
+    MoveParams p;
+    std::memset(&p, 0, sizeof(p));
+    const kvx_cache_desc& s0 = sources[0].src;
+    p.src_base = s0.base;
+    p.src_kv_stride = s0.kv_stride;
+    p.src_layer_stride = s0.layer_stride;
+    p.src_block_stride = s0.block_stride;
+    p.src_num_blocks = s0.num_blocks;
+    p.chunk_bytes = dst->chunk_bytes;
+    p.tile_bytes = lp.tile_bytes;
+    p.tiles_per_chunk = (dst->chunk_bytes + lp.tile_bytes - 1) / lp.tile_bytes;
+    p.num_layers = dst->num_layers;
+    p.num_segs = num_sources;
+    p.status = status_dev;
+    for (int s = 0; s < num_sources; ++s) {
+        const kvx_pull_source& src = sources[s];
+        const MailboxLayout ms = mailbox_layout(src.src_mailbox.max_peers, src.src_mailbox.max_blocks);
+        SegParams& g = p.seg[s];
+        g.src_base = src.src.base;
+        g.src_kv_stride = src.src.kv_stride;
+        g.src_layer_stride = src.src.layer_stride;
+        g.src_block_stride = src.src.block_stride;
+        g.src_num_blocks = src.src.num_blocks;
+        g.dst_base = dst->base;
+        g.dst_kv_stride = dst->kv_stride;
+        g.dst_layer_stride = dst->layer_stride;
+        g.dst_block_stride = dst->block_stride;
+        g.dst_num_blocks = dst->num_blocks;
+        g.src_ids = src.src_ids_dev;
+        g.dst_ids = src.dst_ids_dev;
+        g.num_ids = src.num_ids;
+        // An empty transfer still signals; give it one id slot of no tiles.
+        g.num_tiles = src.num_ids * 2 * static_cast<int64_t>(dst->num_layers) * p.tiles_per_chunk;
+        if (src.num_ids == 0) g.num_ids = 1;
+        g.go = nullptr;
+        g.token = src.token;
+        g.counter = mb_ptr<unsigned int>(my_mb, m.pull_counter, src.src_rank);
+        g.flag = mb_ptr<uint64_t>(&src.src_mailbox, ms.pulled, my_rank);
+    }
+    assign_ctas(p, lp.grid);
+    LaunchPlan run = lp;
+    run.grid = total_ctas(p);
+    return launch_move(device, p, run, static_cast<cudaStream_t>(stream));
+}
+
+int kvx_pair_wait_pulled(int32_t device, const kvx_mailbox* my_mb, int32_t dst_rank, uint64_t timeout_ns,
+                         int32_t* status_dev, void* stream) {
+    int rc = check_mailbox(my_mb, "local");
+    if (rc) return rc;
+    if (dst_rank < 0 || dst_rank >= my_mb->max_peers) return fail(KVX_EINVAL, "dst_rank out of range");
+    if (status_dev == nullptr) return fail(KVX_EINVAL, "status_dev is NULL");
+    KVX_DEVICE_GUARD(device);
+    const MailboxLayout m = mailbox_layout(my_mb->max_peers, my_mb->max_blocks);
+    wait_pulled_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        mb_ptr<uint64_t>(my_mb, m.pulled, dst_rank), mb_ptr<uint64_t>(my_mb, m.pull_consumed, dst_rank), timeout_ns,
+        status_dev);
+    KVX_CUDA(cudaGetLastError(), "launch wait-pulled kernel");
+    return KVX_OK;
 }
 
 int kvx_ipc_export(int32_t device, const void* dev_ptr, void* handle_out_64, uint64_t* offset_out) {

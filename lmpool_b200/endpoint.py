@@ -109,6 +109,7 @@ class TransferEndpoint:
         self._ipc_maps: dict[bytes, list] = {}   # handle -> [base address, references]
         # word 0: this endpoint's per-call status (zeroed per transfer)
         self.status = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
+        self.mode = "pull"          # pair transfer mode used by exchange(); the same on every rank
         self.closed = False
 
     # -- local cache ---------------------------------------------------------
@@ -272,6 +273,76 @@ class TransferEndpoint:
                                                self.rank, arr, len(group), ctypes.c_void_p(self.status.data_ptr()),
                                                ctypes.c_void_p(_capi.stream_handle(stream))),
                         "kvx_pair_push")
+
+    def pull(self, local: CacheLayout, sources: list[tuple], stream) -> None:
+        """Destination-driven copy: one launch per group of up to 8 sources,
+        each (link, peer layout, src ids, dst ids, count, token)."""
+        dst_desc = local.desc()
+        for start in range(0, len(sources), MAX_TARGETS_PER_LAUNCH):
+            group = sources[start:start + MAX_TARGETS_PER_LAUNCH]
+            arr = (_capi.PullSource * len(group))()
+            for k, (link, peer_layout, sids, dids, n, token) in enumerate(group):
+                arr[k].src = peer_layout.desc()
+                arr[k].src_mailbox = link.mailbox
+                arr[k].src_ids_dev = sids.data_ptr() if n else 0
+                arr[k].dst_ids_dev = dids.data_ptr() if n else 0
+                arr[k].num_ids = n
+                arr[k].token = token
+                arr[k].src_rank = link.peer
+                arr[k].reserved = 0
+            _capi.check(self.lib.kvx_pair_pull(self.device, ctypes.byref(dst_desc), ctypes.byref(self.mailbox),
+                                               self.rank, arr, len(group), ctypes.c_void_p(self.status.data_ptr()),
+                                               ctypes.c_void_p(_capi.stream_handle(stream))),
+                        "kvx_pair_pull")
+
+    def wait_pulled(self, dst_rank: int, timeout_s: float | None, stream) -> None:
+        _capi.check(self.lib.kvx_pair_wait_pulled(self.device, ctypes.byref(self.mailbox), dst_rank,
+                                                  timeout_ns(timeout_s), ctypes.c_void_p(self.status.data_ptr()),
+                                                  ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_pair_wait_pulled")
+
+    def exchange(self, mode: str, local: CacheLayout, outgoing: list[tuple], incoming: list[tuple],
+                 timeout_s: float | None, stream, peer_layouts: dict | None = None) -> None:
+        """Enqueue every transfer of this rank (no host wait).
+
+        ``outgoing`` = [(dst_rank, src ids, count)] of blocks this rank gives;
+        ``incoming`` = [(src_rank, src ids, dst ids, count)] of blocks it
+        receives (src ids are used in pull mode only). ``peer_layouts`` maps a
+        rank to the peer layout to read or write (default: the peer's cache).
+        Push: arms for every incoming transfer first, then one push launch
+        for all outgoing ones, then the completion waits. Pull: one pull
+        launch for all incoming transfers, then the waits for the peers that
+        read this rank's blocks. Either order leaves no wait depending on a
+        later launch of any rank.
+        """
+        layouts = peer_layouts or {}
+        if mode == "push":
+            tokens = []
+            for src_rank, _sids, dids, n in incoming:
+                token = self.next_token(src_rank)
+                self.publish(self.get_link(src_rank), dids, n, token, stream)
+                tokens.append((src_rank, token))
+            targets = []
+            for dst_rank, sids, n in outgoing:
+                link = self.get_link(dst_rank)
+                self.wait_armed(link, n, timeout_s, stream)
+                targets.append((link, layouts.get(dst_rank, link.cache), sids, n))
+            if targets:
+                self.push(local, targets, stream)
+            for src_rank, token in tokens:
+                self.wait_done(src_rank, token, timeout_s, stream)
+        elif mode == "pull":
+            sources = []
+            for src_rank, sids, dids, n in incoming:
+                link = self.get_link(src_rank)
+                sources.append((link, layouts.get(src_rank, link.cache), sids, dids, n, self.next_token(src_rank)))
+            if sources:
+                self.pull(local, sources, stream)
+            for dst_rank, _sids, _n in outgoing:
+                self.get_link(dst_rank)
+                self.wait_pulled(dst_rank, timeout_s, stream)
+        else:
+            raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull' or 'push'")
 
     def read_done(self, src_rank: int) -> int:
         out = ctypes.c_uint64(0)

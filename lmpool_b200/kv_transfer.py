@@ -414,30 +414,26 @@ def register_kv_cache(kv_cache, num_layers: int | None = None) -> CacheLayout:
     return lay
 
 
+def transfer_mode() -> str:
+    """Pair transfer mode of this process: ``pull`` (default: the destination
+    reads the source's blocks over NVLink) or ``push`` (the source writes into
+    the destination's blocks), from ``LMPOOL_B200_KV_MODE``. Every rank of a
+    world must use the same mode; prewarm checks it."""
+    mode = os.environ.get("LMPOOL_B200_KV_MODE", "pull").strip().lower()
+    if mode not in ("pull", "push"):
+        raise RuntimeError(f"LMPOOL_B200_KV_MODE must be 'pull' or 'push', got {mode!r}")
+    return mode
+
+
 def _endpoint(rank: int, world_size: int, device: int, max_blocks: int) -> TransferEndpoint:
     ep = _ENDPOINTS.get(device)
     if ep is not None and (ep.rank != rank or ep.world_size != world_size or ep.mailbox.max_blocks < max_blocks):
         raise RuntimeError("transfer endpoint was set up for another world; call shutdown() first")
     if ep is None:
         ep = TransferEndpoint(rank, world_size, device, max_blocks)
+        ep.mode = transfer_mode()
         _ENDPOINTS[device] = ep
     return ep
-
-
-def shutdown(barrier: bool = True) -> None:
-    """Close peer mappings, then free mailboxes (tests, orderly exit).
-
-    With a process group, every rank unmaps its peers before any rank frees
-    its own mailbox (a collective: all ranks call it together).
-    """
-    for ep in list(_ENDPOINTS.values()):
-        ep.close_links()
-    if barrier and dist.is_available() and dist.is_initialized():
-        dist.barrier()
-    for ep in list(_ENDPOINTS.values()):
-        ep.close()
-    _ENDPOINTS.clear()
-    _P2P_GROUPS.clear()
 
 
 def prewarm_p2p_pairs(
@@ -487,9 +483,13 @@ def prewarm_p2p_pairs(
                                payload.data_ptr())
     rec = ep.export_record(hostname=socket.gethostname())
     pl_handle, pl_off = ep.export_buffer(payload.data_ptr())
-    rec.extra = {"payload_handle": pl_handle, "payload_offset": pl_off, "payload_ptr": payload.data_ptr()}
+    rec.extra = {"payload_handle": pl_handle, "payload_offset": pl_off, "payload_ptr": payload.data_ptr(),
+                 "mode": ep.mode}
     records: list = [None] * world_size
     dist.all_gather_object(records, rec)
+    modes = {r.extra.get("mode") for r in records}
+    if len(modes) != 1:
+        raise RuntimeError(f"ranks disagree on the transfer mode (LMPOOL_B200_KV_MODE): {sorted(map(str, modes))}")
 
     payload_maps: dict[int, CacheLayout] = {}
     payload_closers: list = []
@@ -511,14 +511,14 @@ def prewarm_p2p_pairs(
         payload.fill_(float(src + 1) if rank == src else 0.0)
         # Warm-up transfer: first touch of the peer mapping and kernels.
         if rank == src:
-            _source_side(ep, dst, pl_layout, payload_maps[dst], ids, timeout_s, stream)
+            _source_side(ep, dst, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[dst])
         elif rank == dst:
-            _destination_side(ep, src, ids, len(ids), timeout_s, stream)
+            _destination_side(ep, src, ids, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[src])
         dist.barrier()
         if rank == src:
             torch.cuda.synchronize(device)
             started = time.perf_counter()
-            _source_side(ep, dst, pl_layout, payload_maps[dst], ids, timeout_s, stream)
+            _source_side(ep, dst, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[dst])
             torch.cuda.synchronize(device)
             observations.append({
                 "src_gpu": src,
@@ -528,7 +528,7 @@ def prewarm_p2p_pairs(
             })
         elif rank == dst:
             payload.fill_(0.0)
-            _destination_side(ep, src, ids, len(ids), timeout_s, stream)
+            _destination_side(ep, src, ids, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[src])
             if not bool(torch.all(payload == float(src + 1)).item()):
                 raise RuntimeError(f"KV transfer P2P prewarm validation failed for pair {(src, dst)}")
         dist.barrier()
@@ -540,27 +540,39 @@ def prewarm_p2p_pairs(
     return observations
 
 
-def _destination_side(ep: TransferEndpoint, src_rank: int, dst_ids: List[int], expected: int,
-                      timeout_s: float | None, stream) -> None:
-    link = ep.get_link(src_rank)
-    token = ep.next_token(src_rank)
-    ids = _ids_tensor(dst_ids, ep.device)
+def _run_exchange(ep: TransferEndpoint, local: CacheLayout, outgoing: list, incoming: list,
+                  timeout_s: float | None, stream, peer_layouts: dict | None, what: str) -> None:
     with torch.cuda.stream(stream):
         ep.status.zero_()
-    ep.publish(link, ids, len(dst_ids), token, stream)
-    ep.wait_done(src_rank, token, timeout_s, stream)
-    ep.check_status(stream, f"transfer {src_rank}->{ep.rank} (destination)", peers=(src_rank,))
+    ep.exchange(ep.mode, local, outgoing, incoming, timeout_s, stream, peer_layouts)
+    peers = [o[0] for o in outgoing] + [i[0] for i in incoming]
+    ep.check_status(stream, what, peers=peers)
 
 
-def _source_side(ep: TransferEndpoint, dst_rank: int, local: CacheLayout, remote: CacheLayout, src_ids: List[int],
-                 timeout_s: float | None, stream) -> None:
-    link = ep.get_link(dst_rank)
-    ids = _ids_tensor(src_ids, ep.device)
-    with torch.cuda.stream(stream):
-        ep.status.zero_()
-    ep.wait_armed(link, len(src_ids), timeout_s, stream)
-    ep.push(local, [(link, remote, ids, len(src_ids))], stream)
-    ep.check_status(stream, f"transfer {ep.rank}->{dst_rank} (source)", peers=(dst_rank,))
+def _destination_side(ep: TransferEndpoint, src_rank: int, src_ids: List[int], dst_ids: List[int],
+                      timeout_s: float | None, stream, local: CacheLayout | None = None,
+                      remote: CacheLayout | None = None) -> None:
+    """Receive ``src_ids`` of ``src_rank`` into ``dst_ids`` (blocks until they are in place)."""
+    sids, dids = _upload(ep.device, stream, _id_array(src_ids), _id_array(dst_ids))
+    layouts = {src_rank: remote} if remote is not None else None
+    _run_exchange(ep, ep.cache if local is None else local, [], [(src_rank, sids, dids, len(dst_ids))], timeout_s,
+                  stream, layouts, f"transfer {src_rank}->{ep.rank} (destination, {ep.mode})")
+
+
+def _source_side(ep: TransferEndpoint, dst_rank: int, src_ids: List[int], timeout_s: float | None, stream,
+                 local: CacheLayout | None = None, remote: CacheLayout | None = None) -> None:
+    """Give ``src_ids`` to ``dst_rank`` (blocks until the destination holds them)."""
+    (sids,) = _upload(ep.device, stream, _id_array(src_ids))
+    layouts = {dst_rank: remote} if remote is not None else None
+    _run_exchange(ep, ep.cache if local is None else local, [(dst_rank, sids, len(src_ids))], [], timeout_s,
+                  stream, layouts, f"transfer {ep.rank}->{dst_rank} (source, {ep.mode})")
+
+
+def _peer_cache(ep: TransferEndpoint, peer: int) -> CacheLayout:
+    link = ep.get_link(peer)
+    if link.cache is None:
+        raise RuntimeError(f"rank {peer} did not register a KV cache")
+    return link.cache
 
 
 def _check_registered(ep: TransferEndpoint, kv_cache, num_layers: int) -> None:
@@ -628,7 +640,8 @@ def swap_in(
             raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
         _check_registered(ep, kv_cache, num_layers)
         _validate(local_blocks, ep.cache.num_blocks, True, "transfer destination")
-        _destination_side(ep, remote_gpu, local_blocks, len(remote_blocks), timeout_s,
+        _validate(remote_blocks, _peer_cache(ep, remote_gpu).num_blocks, False, "transfer source")
+        _destination_side(ep, remote_gpu, list(remote_blocks), local_blocks, timeout_s,
                           torch.cuda.current_stream(ep.device))
     elif rank == remote_gpu and rank != local_gpu:
         ep = _ENDPOINTS.get(_local_device(rank))
@@ -636,11 +649,8 @@ def swap_in(
             raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
         _check_registered(ep, kv_cache, num_layers)
         _validate(remote_blocks, ep.cache.num_blocks, False, "transfer source")
-        link = ep.get_link(local_gpu)
-        if link.cache is None:
-            raise RuntimeError(f"rank {local_gpu} did not register a KV cache")
-        _source_side(ep, local_gpu, ep.cache, link.cache, list(remote_blocks), timeout_s,
-                     torch.cuda.current_stream(ep.device))
+        _peer_cache(ep, local_gpu)
+        _source_side(ep, local_gpu, list(remote_blocks), timeout_s, torch.cuda.current_stream(ep.device))
     return local_blocks
 
 
@@ -688,68 +698,61 @@ def swap_out(
             raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
         _check_registered(ep, kv_cache, num_layers)
         _validate(blocks_to_evict, ep.cache.num_blocks, False, "transfer source")
-        link = ep.get_link(target_gpu)
-        _source_side(ep, target_gpu, ep.cache, link.cache, list(blocks_to_evict), timeout_s,
-                     torch.cuda.current_stream(ep.device))
+        _peer_cache(ep, target_gpu)
+        _source_side(ep, target_gpu, list(blocks_to_evict), timeout_s, torch.cuda.current_stream(ep.device))
     elif rank == target_gpu and rank != local_gpu:
         ep = _ENDPOINTS.get(_local_device(rank))
         if ep is None:
             raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
         _check_registered(ep, kv_cache, num_layers)
         _validate(target_blocks, ep.cache.num_blocks, True, "transfer destination")
-        _destination_side(ep, local_gpu, target_blocks, len(blocks_to_evict), timeout_s,
+        _validate(blocks_to_evict, _peer_cache(ep, local_gpu).num_blocks, False, "transfer source")
+        _destination_side(ep, local_gpu, list(blocks_to_evict), target_blocks, timeout_s,
                           torch.cuda.current_stream(ep.device))
     return target_blocks
 
 
-def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, List[int]]],
+def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, List[int], List[int]]],
                kv_cache=None, num_layers: int | None = None, timeout_s: float | None = None,
                stream=None, synchronize: bool = True) -> None:
     """Several transfers of this rank at once, in either direction.
 
-    ``outgoing`` = [(dst_rank, src_block_ids)], ``incoming`` =
-    [(src_rank, local_target_block_ids)]. Every incoming arm is published
-    before anything waits, and all outgoing transfers share one push launch
-    (up to 8 destinations per launch), so a rank that both sends and receives
+    ``outgoing`` = [(dst_rank, src_block_ids)] of blocks this rank gives;
+    ``incoming`` = [(src_rank, src_block_ids, local_target_block_ids)] of
+    blocks it receives. All incoming transfers share one launch and all
+    outgoing ones are only waited on, so a rank that both sends and receives
     cannot deadlock against its peers (two sequential ``swap_in`` calls in
-    opposite directions would: each source waits for its peer's arm).
+    opposite directions would, with each side waiting for the other).
     """
     device = _local_device(dist.get_rank())
     ep = _ENDPOINTS.get(device)
     if ep is None:
         raise RuntimeError("prewarm_p2p_pairs has not run on this rank")
-    if kv_cache is not None:
-        _check_registered(ep, kv_cache, num_layers if num_layers is not None else ep.cache.num_layers)
     if ep.cache is None:
         raise RuntimeError("no KV cache registered on this rank")
+    if kv_cache is not None:
+        _check_registered(ep, kv_cache, num_layers if num_layers is not None else ep.cache.num_layers)
     stream = torch.cuda.current_stream(device) if stream is None else stream
-    peers = []
+    arrays, out_spec, in_spec = [], [], []
+    for dst_rank, src_ids in outgoing:
+        arrays.append(_validate(src_ids, ep.cache.num_blocks, False, "transfer source"))
+        _peer_cache(ep, dst_rank)
+        out_spec.append((dst_rank, len(arrays) - 1, len(src_ids)))
+    for src_rank, src_ids, dst_ids in incoming:
+        if len(src_ids) != len(dst_ids):
+            raise RuntimeError(f"transfer from rank {src_rank}: {len(src_ids)} source ids, {len(dst_ids)} targets")
+        arrays.append(_validate(src_ids, _peer_cache(ep, src_rank).num_blocks, False, "transfer source"))
+        arrays.append(_validate(dst_ids, ep.cache.num_blocks, True, "transfer destination"))
+        in_spec.append((src_rank, len(arrays) - 2, len(arrays) - 1, len(dst_ids)))
+    dev_ids = _upload(device, stream, *arrays) if arrays else []
+    out = [(d, dev_ids[i], n) for d, i, n in out_spec]
+    inc = [(s_, dev_ids[i], dev_ids[j], n) for s_, i, j, n in in_spec]
     with torch.cuda.stream(stream):
         ep.status.zero_()
-    tokens = []
-    for src_rank, dst_ids in incoming:
-        _validate(dst_ids, ep.cache.num_blocks, True, "transfer destination")
-        link = ep.get_link(src_rank)
-        token = ep.next_token(src_rank)
-        ids = _ids_tensor(dst_ids, device)
-        ep.publish(link, ids, len(dst_ids), token, stream)
-        tokens.append((src_rank, token, ids))
-        peers.append(src_rank)
-    targets = []
-    for dst_rank, src_ids in outgoing:
-        _validate(src_ids, ep.cache.num_blocks, False, "transfer source")
-        link = ep.get_link(dst_rank)
-        if link.cache is None:
-            raise RuntimeError(f"rank {dst_rank} did not register a KV cache")
-        ep.wait_armed(link, len(src_ids), timeout_s, stream)
-        targets.append((link, link.cache, _ids_tensor(src_ids, device), len(src_ids)))
-        peers.append(dst_rank)
-    if targets:
-        ep.push(ep.cache, targets, stream)
-    for src_rank, token, _ids in tokens:
-        ep.wait_done(src_rank, token, timeout_s, stream)
+    ep.exchange(ep.mode, ep.cache, out, inc, timeout_s, stream)
     if synchronize:
-        ep.check_status(stream, f"swap_batch on rank {ep.rank}", peers=peers)
+        ep.check_status(stream, f"swap_batch on rank {ep.rank} ({ep.mode})",
+                        peers=[o[0] for o in out] + [i[0] for i in inc])
 
 
 # ---------------------------------------------------------------------------

@@ -344,9 +344,10 @@ def _fake_runner(rank: int, cache: torch.Tensor):
     return r
 
 
-def _api_worker(rank: int, port: int, queue) -> None:
+def _api_worker(rank: int, port: int, queue, mode: str = "pull") -> None:
     """Rest of the drop-in surface across two processes: ModelRunner mixin,
     negotiated swap_in, legacy swap_out, swap_batch both ways at once."""
+    os.environ["LMPOOL_B200_KV_MODE"] = mode
     import torch.distributed as dist
 
     from lmpool_b200 import kv_transfer as kt
@@ -407,9 +408,9 @@ def _api_worker(rank: int, port: int, queue) -> None:
         out0, out1 = perm[:7], perm[7:14]          # sources on ranks 0 and 1
         in1, in0 = perm[20:27], perm[27:34]         # targets on ranks 1 and 0 (disjoint from the sources)
         if rank == 0:
-            kt.swap_batch([(1, out0)], [(0 + 1, in0)], timeout_s=20)
+            kt.swap_batch([(1, out0)], [(1, out1, in0)], timeout_s=20)
         else:
-            kt.swap_batch([(0, out1)], [(0, in1)], timeout_s=20)
+            kt.swap_batch([(0, out1)], [(0, out0, in1)], timeout_s=20)
         new0, new1 = model[0].clone(), model[1].clone()
         c_oracle.swap_planned(model[0], out0, new1, in1, nthreads=4)
         c_oracle.swap_planned(model[1], out1, new0, in0, nthreads=4)
@@ -424,11 +425,12 @@ def _api_worker(rank: int, port: int, queue) -> None:
 
 
 @pytest.mark.skipif(device_count() < 2, reason="needs 2 GPUs")
-def test_two_processes_drop_in_api_surface(require_gpu):
+@pytest.mark.parametrize("mode", ["pull", "push"])
+def test_two_processes_drop_in_api_surface(require_gpu, mode):
     ctx = mp.get_context("spawn")
     port = _free_port()
     queue = ctx.Queue()
-    procs = [ctx.Process(target=_api_worker, args=(r, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_api_worker, args=(r, port, queue, mode)) for r in range(2)]
     for p in procs:
         p.start()
     results = []
@@ -448,3 +450,121 @@ def test_two_processes_drop_in_api_surface(require_gpu):
                 p.join(timeout=10)
     assert len(results) == 2, results
     assert all(not r["errors"] for r in results), results
+
+
+# -- destination-driven (pull) mode ------------------------------------------------
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])
+def test_loopback_pull_on_one_stream(require_gpu, variant):
+    """Rank 1 pulls rank 0's blocks (same GPU) and signals rank 0, which waits
+    afterwards on the same stream; three rounds on one pair."""
+    lib = require_gpu
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(ctypes.byref(old))
+    lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=variant)))
+    try:
+        shape = (2, 36, 24, 256, 8, 128)
+        src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 15)
+        s = torch.cuda.current_stream(0)
+        for round_ in range(3):
+            src_ids = kvgen.seeded_perm(24, 70 + round_)[:8]
+            src_ids[3] = src_ids[0]                          # a repeated source id is legal
+            dst_ids = kvgen.seeded_perm(24, 80 + round_)[:8]
+            ep0.status.zero_()
+            ep1.status.zero_()
+            token = ep1.next_token(0)
+            ep1.pull(ep1.cache, [(link10, link10.cache, _ids(src_ids, 0), _ids(dst_ids, 0), 8, token)], s)
+            ep0.wait_pulled(1, 5.0, s)
+            ep1.check_status(s, "destination")
+            ep0.check_status(s, "source")
+            c_oracle.swap_planned(src_cpu, src_ids, dst_cpu, dst_ids, nthreads=4)
+            assert _same_bits(dst, dst_cpu)
+            assert _same_bits(src, src_cpu)
+        ep0.close()
+        ep1.close()
+    finally:
+        lib.kvx_set_tuning(ctypes.byref(old))
+
+
+def test_one_pull_launch_reads_several_sources(require_gpu):
+    shape = (2, 5, 20, 64, 4, 64)
+    N = shape[2]
+    cpus = [kvgen.seeded_cache(shape, 600 + r) for r in range(4)]
+    gpus = [c.to("cuda:0") for c in cpus]
+    eps = [TransferEndpoint(r, 4, 0, N) for r in range(4)]
+    for r in range(4):
+        eps[r].set_cache(affine_layout(gpus[r], shape[1]), gpus[r])
+    recs = [e.export_record() for e in eps]
+    to_src = {r: eps[3].link(recs[r]) for r in (0, 1, 2)}
+    for r in (0, 1, 2):
+        eps[r].link(recs[3])
+    s = torch.cuda.current_stream(0)
+    counts = {0: 6, 1: 0, 2: 4}
+    perm = kvgen.seeded_perm(N, 610)
+    dst_ids = {0: perm[0:6], 1: [], 2: perm[6:10]}                # disjoint targets
+    src_ids = {r: kvgen.seeded_perm(N, 620 + r)[:counts[r]] for r in (0, 1, 2)}
+    for e in eps:
+        e.status.zero_()
+    eps[3].pull(eps[3].cache, [(to_src[r], to_src[r].cache, _ids(src_ids[r], 0), _ids(dst_ids[r], 0), counts[r],
+                                eps[3].next_token(r)) for r in (0, 1, 2)], s)
+    for r in (0, 1, 2):
+        eps[r].wait_pulled(3, 5.0, s)
+    for e in eps:
+        e.check_status(s, f"rank {e.rank}")
+    for r in (0, 1, 2):
+        c_oracle.swap_planned(cpus[r], src_ids[r], cpus[3], dst_ids[r], nthreads=4)
+    assert _same_bits(gpus[3], cpus[3])
+    for r in (0, 1, 2):
+        assert _same_bits(gpus[r], cpus[r])
+    for e in eps:
+        e.close_links()
+    for e in eps:
+        e.close()
+
+
+def test_wait_pulled_times_out_and_stale_pulls_do_not_count(require_gpu):
+    shape = (2, 2, 8, 16, 1, 64)
+    _, _, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 16)
+    s = torch.cuda.current_stream(0)
+    ep0.status.zero_()
+    ep0.wait_pulled(1, 0.2, s)                  # nothing pulled yet
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep0.check_status(s, "source")
+    ep0.status.zero_()
+    ep1.status.zero_()
+    ids = _ids([1, 2], 0)
+    ep1.pull(ep1.cache, [(link10, link10.cache, ids, ids, 2, ep1.next_token(0))], s)
+    ep0.wait_pulled(1, 2.0, s)                  # consumes that pull
+    ep0.check_status(s, "first")
+    ep0.wait_pulled(1, 0.2, s)                  # the same pull cannot satisfy a second wait
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep0.check_status(s, "second")
+    ep0.close()
+    ep1.close()
+
+
+@pytest.mark.skipif(device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])
+def test_two_gpus_one_process_pull_over_nvlink(require_gpu, variant):
+    lib = require_gpu
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(ctypes.byref(old))
+    lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=variant)))
+    try:
+        shape = (2, 36, 64, 256, 8, 128)
+        src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 1, shape, 17)
+        s0, s1 = torch.cuda.current_stream(0), torch.cuda.current_stream(1)
+        src_ids = kvgen.seeded_perm(64, 18)[:16]
+        dst_ids = kvgen.seeded_perm(64, 19)[:16]
+        ep0.status.zero_()
+        ep1.status.zero_()
+        ep1.pull(ep1.cache, [(link10, link10.cache, _ids(src_ids, 1), _ids(dst_ids, 1), 16, ep1.next_token(0))], s1)
+        ep0.wait_pulled(1, 10.0, s0)
+        ep1.check_status(s1, "destination")
+        ep0.check_status(s0, "source")
+        c_oracle.swap_planned(src_cpu, src_ids, dst_cpu, dst_ids, nthreads=8)
+        assert _same_bits(dst, dst_cpu)
+        ep0.close()
+        ep1.close()
+    finally:
+        lib.kvx_set_tuning(ctypes.byref(old))
