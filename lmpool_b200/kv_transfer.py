@@ -436,6 +436,23 @@ def _endpoint(rank: int, world_size: int, device: int, max_blocks: int) -> Trans
     return ep
 
 
+def shutdown(barrier: bool = True) -> None:
+    """Close peer mappings, then free mailboxes (tests, orderly exit).
+
+    With a process group, every rank unmaps its peers before any rank frees
+    its own mailbox (a collective: all ranks call it together); CUDA forbids
+    freeing exported memory while another process still maps it.
+    """
+    for ep in list(_ENDPOINTS.values()):
+        ep.close_links()
+    if barrier and dist.is_available() and dist.is_initialized():
+        dist.barrier()
+    for ep in list(_ENDPOINTS.values()):
+        ep.close()
+    _ENDPOINTS.clear()
+    _P2P_GROUPS.clear()
+
+
 def prewarm_p2p_pairs(
     pairs: Iterable[tuple[int, int]],
     *,

@@ -126,3 +126,24 @@ def test_move_blocks_count_mismatch_raises():
 
 def test_prewarm_without_process_group_returns_empty():
     assert kt.prewarm_p2p_pairs([(0, 1)]) == []
+
+
+def test_drop_in_module_exposes_the_reference_names_and_ours():
+    # every name of src/lmpool/engine/kv_transfer.py, plus this package's additions
+    reference = ["_normalize_transfer_pairs", "_pair_group", "prewarm_p2p_pairs", "_allocate_empty_block",
+                 "_compute_tag", "_get_layer_kv", "_pack_layer_blocks", "_unpack_layer_blocks", "_empty_layer_payload",
+                 "_pack_all_layer_blocks", "_empty_all_layer_payload", "_unpack_all_layer_blocks", "_send_block_list",
+                 "_recv_block_list", "swap_out", "swap_in", "request_free_blocks", "respond_free_blocks", "_P2P_GROUPS"]
+    ours = ["register_kv_cache", "move_blocks", "swap_batch", "check_device_status", "shutdown", "transfer_mode"]
+    missing = [n for n in reference + ours if not hasattr(kt, n)]
+    assert not missing, missing
+
+
+def test_transfer_mode_defaults_to_pull_and_validates(monkeypatch):
+    monkeypatch.delenv("LMPOOL_B200_KV_MODE", raising=False)
+    assert kt.transfer_mode() == "pull"
+    monkeypatch.setenv("LMPOOL_B200_KV_MODE", "push")
+    assert kt.transfer_mode() == "push"
+    monkeypatch.setenv("LMPOOL_B200_KV_MODE", "sideways")
+    with pytest.raises(RuntimeError, match="pull"):
+        kt.transfer_mode()
