@@ -442,7 +442,7 @@ def block_sums(cache: torch.Tensor, ids: list[int]) -> torch.Tensor:
     return out.cpu()
 
 
-def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
+def pair_sweep(ep, link, g: dict, rank: int, stream, dist, mode: str) -> list[dict]:
     """BASELINE config 3 on ranks 0 -> 1: B in {1, 8, 64, 256}, contiguous and
     scattered source ids. Each timed run is K back-to-back transfers in the
     configured mode, cycling through disjoint id sets so no transfer re-reads
@@ -451,11 +451,11 @@ def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
     N = g["N"]
     out = []
     for B in (1, 8, 64, 256):
-        for mode in ("contiguous", "scattered"):
+        for ids_kind in ("contiguous", "scattered"):
             K = 20 if B <= 64 else 8
             nsets = max(1, min(K, (N // 2) // B))
             gen = torch.Generator().manual_seed(3000 + B)
-            if mode == "contiguous":
+            if ids_kind == "contiguous":
                 starts = torch.randint(0, N - B, (nsets,), generator=gen).tolist()
                 src_sets = [list(range(st, st + B)) for st in starts]
             else:
@@ -468,9 +468,9 @@ def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
 
             def one(k):
                 if rank == 1:
-                    ep.exchange(ep.mode, ep.cache, [], [(0, src_t[k % nsets], dst_t[k % nsets], B)], 60.0, stream)
+                    ep.exchange(mode, ep.cache, [], [(0, src_t[k % nsets], dst_t[k % nsets], B)], 60.0, stream)
                 else:
-                    ep.exchange(ep.mode, ep.cache, [(1, src_t[k % nsets], B)], [], 60.0, stream)
+                    ep.exchange(mode, ep.cache, [(1, src_t[k % nsets], B)], [], 60.0, stream)
 
             for k in range(3):
                 one(k)
@@ -487,7 +487,8 @@ def pair_sweep(ep, link, g: dict, rank: int, stream, dist) -> list[dict]:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
             pb = payload_bytes(g, B)
-            out.append({"blocks": B, "ids": mode, "bytes": pb, "ms": ms, "GB/s": pb / (ms * 1e-3) / 1e9,
+            out.append({"mode": mode, "blocks": B, "ids": ids_kind, "bytes": pb, "ms": ms,
+                        "GB/s": pb / (ms * 1e-3) / 1e9,
                         "frac_nvlink": pb / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS})
     return out
 
@@ -537,7 +538,7 @@ def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, B: int = 6
             "blocks": B, "ms": ms, "GB/s": P / (ms * 1e-3) / 1e9}
 
 
-def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist) -> dict:
+def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: str) -> dict:
     """BASELINE config 4 phase B: every rank sends B=32 seeded-random blocks to
     every other rank at once, into disjoint reserved sets; one push launch per
     rank carries all its destinations."""
@@ -564,7 +565,7 @@ def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist) -> dict
     psrc_t = {s: torch.tensor(v, dtype=torch.int64, device=dev) for s, v in peer_out.items()}
 
     def step():
-        ep.exchange(ep.mode, ep.cache, [(d, out_t[d], B) for d in peers],
+        ep.exchange(mode, ep.cache, [(d, out_t[d], B) for d in peers],
                     [(s, psrc_t[s], in_t[s], B) for s in peers], 60.0, stream)
 
     ep.status.zero_()
@@ -633,15 +634,18 @@ def bench_pairs(args) -> dict | None:
     dst_ids = free[:B]
     ep = kt._ENDPOINTS[local]
     link = ep.get_link(partner)
-    mode = ep.mode
+    # Both directions of a pair at once: push measured faster (pull's read
+    # requests share each direction with the other flow's data).
+    mode = "push" if args.pair_mode == "auto" else args.pair_mode
+    other = "pull" if mode == "push" else "push"
     stream = torch.cuda.current_stream(dev)
     src_t = torch.tensor(src_ids, dtype=torch.int64, device=dev)
     psrc_t = torch.tensor(partner_src, dtype=torch.int64, device=dev)
     dst_t = torch.tensor(dst_ids, dtype=torch.int64, device=dev)
     P = payload_bytes(g, B)
 
-    def step():
-        ep.exchange(mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, stream)
+    def step(m=None):
+        ep.exchange(m or mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, stream)
 
     ep.status.zero_()
     for _ in range(args.warmup):
@@ -671,24 +675,44 @@ def bench_pairs(args) -> dict | None:
     ok = all(item["bits"] == 0 for item in gathered)
     ok &= torch.equal(gathered[partner]["src"], sums_dst)
 
-    sweep = pair_sweep(ep, link, g, rank, stream, dist) if world == 2 else None
+    # the same exchange in the other mode, for the record
+    for _ in range(3):
+        step(other)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(10):
+        step(other)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 10], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    other_ms = float(t.item())
+
+    sweep = None
+    if world == 2:   # one direction at a time: both modes, pull is the default of swap_in
+        sweep = pair_sweep(ep, link, g, rank, stream, dist, "pull") + pair_sweep(ep, link, g, rank, stream, dist,
+                                                                               "push")
     ref_pair = reference_gpu_pair(cache, g, rank, dist) if world == 2 else None
     if ref_pair is not None and sweep is not None:
-        mine = next(r for r in sweep if r["blocks"] == ref_pair["blocks"] and r["ids"] == "scattered")
-        ref_pair["this_kernel_speedup"] = ref_pair["ms"] / mine["ms"]
-    phase_b = all_partner(ep, cache, g, rank, world, stream, dist) if world >= 4 else None
-    ok &= phase_b is None or phase_b["ok"]
+        best = min(r["ms"] for r in sweep if r["blocks"] == ref_pair["blocks"] and r["ids"] == "scattered")
+        ref_pair["this_kernel_speedup"] = ref_pair["ms"] / best
+    phase_b = None
+    if world >= 4:
+        phase_b = {m: all_partner(ep, cache, g, rank, world, stream, dist, m) for m in ("push", "pull")}
+        ok &= all(v["ok"] for v in phase_b.values())
 
     # end to end: host id lists through swap_batch (pinned H2D + status D2H per step)
     e2e_steps = max(3, min(args.steps, 30))
     for _ in range(2):
-        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)])
+        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode)
     dist.barrier()
     torch.cuda.synchronize()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(e2e_steps):
-        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)])
+        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode)
     e3.record(stream)
     torch.cuda.synchronize()
     t2 = torch.tensor([e2.elapsed_time(e3) / e2e_steps], dtype=torch.float64, device=dev)
@@ -722,10 +746,12 @@ def bench_pairs(args) -> dict | None:
                 "api": "lmpool_b200.kv_transfer.swap_batch(host id lists)"},
         "gpu_launches": (4 if mode == "push" else 2) * args.steps,
         "transfer_mode": mode,
+        "other_mode": {"mode": other, "ms_per_step": other_ms,
+                       "GB/s_per_direction": P / (other_ms * 1e-3) / 1e9},
         "clocks": merge_clocks([item["clk"] for item in gathered]),
         "pair_sweep": sweep,
         "reference_gpu_path": ref_pair,
-        "phase_b": ({k: v for k, v in phase_b.items() if k != "ok"} if phase_b else None),
+        "phase_b": ({m: {k: v for k, v in r.items() if k != "ok"} for m, r in phase_b.items()} if phase_b else None),
     }
 
 
@@ -872,8 +898,10 @@ def bench_config5(args) -> dict | None:
 
     psrc_t = torch.tensor(seeded_perm(c["N"], 7000 + partner)[:B], dtype=torch.int64, device=dev)
 
+    mode = "push" if args.pair_mode == "auto" else args.pair_mode   # both directions at once
+
     def xfer():
-        ep.exchange(ep.mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, xs)
+        ep.exchange(mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, xs)
 
     def store_step():
         with torch.cuda.stream(ss):
@@ -946,7 +974,7 @@ def bench_config5(args) -> dict | None:
         "overlapped": {"transfers": K, "store_steps": M, "transfer_ms": xo_ms,
                        "transfer_GB/s_per_direction": P / (xo_ms * 1e-3) / 1e9,
                        "store_ms_per_step": so_ms, "store_GB/s": store_bytes / (so_ms * 1e-3) / 1e9},
-        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes, "transfer_mode": ep.mode,
+        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes, "transfer_mode": mode,
     }
 
 
@@ -964,6 +992,8 @@ def main() -> None:
                     help="config5: BASELINE config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
                          "pair1p: one process, two GPUs, pair push (profiling); store: store_kvcache only")
     ap.add_argument("--pull", action="store_true", help="pair1p: destination pulls instead of source pushing")
+    ap.add_argument("--pair-mode", choices=["auto", "push", "pull"], default="auto",
+                    help="N>1 exchanges that send both ways at once (phase A, config 5): auto = push")
     ap.add_argument("--quick", action="store_true",
                     help="1 GPU: time the headline loop only (no sweep, e2e or CPU baseline); for profiling")
     args = ap.parse_args()
