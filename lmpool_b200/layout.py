@@ -271,9 +271,3 @@ def payload_layout(num_layers: int, num_blocks: int, block_shape, dtype, device,
         device=torch.device(device),
         block_shape=tuple(int(s) for s in block_shape),
     )
-
-
-def layer_payload_layout(num_blocks: int, block_shape, dtype, device, base: int) -> CacheLayout:
-    """Layout of a one-layer payload ``[2, B, *block_shape]`` (kv_transfer.py:186-196)."""
-    lay = payload_layout(1, num_blocks, block_shape, dtype, device, base)
-    return lay
