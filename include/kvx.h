@@ -47,7 +47,7 @@
 extern "C" {
 #endif
 
-#define KVX_ABI_VERSION 2
+#define KVX_ABI_VERSION 1
 
 /* ---- host status codes ------------------------------------------------- */
 #define KVX_OK 0
@@ -116,7 +116,6 @@ typedef struct kvx_tuning {
     int32_t ctas_per_sm;   /* 0 = automatic */
     int32_t tile_bytes;    /* 0 = automatic; else multiple of 16 */
     int32_t stages;        /* TMA ring depth; 0 = automatic */
-    int32_t store_layer_group; /* layers per warp of the all-layer store: 0 = automatic, 1, 2, 4 or 8 */
 } kvx_tuning;
 
 /* ---- library ------------------------------------------------------------ */

@@ -16,7 +16,7 @@ import threading
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent / "_kvx.so"
-ABI_VERSION = 2
+ABI_VERSION = 1
 
 KVX_OK = 0
 KVX_EINVAL = 1
@@ -115,7 +115,6 @@ class Tuning(ctypes.Structure):
         ("ctas_per_sm", ctypes.c_int32),
         ("tile_bytes", ctypes.c_int32),
         ("stages", ctypes.c_int32),
-        ("store_layer_group", ctypes.c_int32),
     ]
 
 

@@ -44,9 +44,6 @@ constexpr int kMaxSegments = 8;
 constexpr int kRegThreads = 256;
 constexpr int kRegUnroll = 4;
 constexpr int kStoreThreads = 256;
-// Layers per warp of the all-layer store when not tuned (1 = one layer per
-// warp, the single-layer kernel's grid).
-constexpr int kStoreAutoLayerGroup = 4;
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kFailBit = 1ull << 63;
 // Upper bound on mbarrier polls of a bulk-copy stage before the pipeline
@@ -420,7 +417,6 @@ struct StoreParams {
     int64_t num_slots;
     int64_t row_bytes;
     int32_t block_size;
-    int32_t num_layers;
     int32_t* status;
 };
 
@@ -457,43 +453,6 @@ __global__ void __launch_bounds__(kStoreThreads) store_kvcache_kernel(const __gr
         d[i + 96] = r3;
     }
     for (; i < n; i += 32) d[i] = ld_stream(s + i);
-}
-
-// All-layer store with LG layers per warp: the token's slot is loaded once
-// and LG rows (one per layer) are in flight per lane before their stores,
-// instead of one dependent slot load + one row per warp. grid.y = layer groups.
-template <int LG>
-__global__ void __launch_bounds__(kStoreThreads) store_kvcache_group_kernel(const __grid_constant__ StoreParams p) {
-    using V = uint4;
-    const int lane = threadIdx.x & 31;
-    const int64_t w = static_cast<int64_t>(blockIdx.x) * (kStoreThreads / 32) + (threadIdx.x >> 5);
-    const int64_t t = w >> 1;
-    const int kv = static_cast<int>(w & 1);
-    if (t >= p.num_tokens) return;
-    const int64_t layer0 = static_cast<int64_t>(blockIdx.y) * LG;
-    const int nl = static_cast<int>(min(static_cast<int64_t>(LG), static_cast<int64_t>(p.num_layers) - layer0));
-    const int64_t slot = __ldg(p.slots + t);
-    if (slot == -1) return;
-    if (slot < -1 || slot >= p.num_slots) {
-        if (lane == 0 && kv == 0) atomicOr(p.status, KVX_DEV_BAD_SLOT);
-        return;
-    }
-    const int64_t blk = slot / p.block_size;
-    const int64_t off = slot - blk * p.block_size;
-    const int64_t in_ls = kv ? p.value_layer_stride : p.key_layer_stride;
-    const int64_t c_ls = kv ? p.vc_layer_stride : p.kc_layer_stride;
-    const char* src = (kv ? p.value + t * p.value_token_stride : p.key + t * p.key_token_stride) + layer0 * in_ls;
-    char* dst = (kv ? p.v_cache : p.k_cache) + layer0 * c_ls + blk * p.block_stride + off * p.slot_stride;
-    const int64_t n = p.row_bytes / 16;
-    for (int64_t i = lane; i < n; i += 32) {
-        V r[LG];
-#pragma unroll
-        for (int l = 0; l < LG; ++l)
-            if (l < nl) r[l] = ld_stream(reinterpret_cast<const V*>(src + l * in_ls) + i);
-#pragma unroll
-        for (int l = 0; l < LG; ++l)
-            if (l < nl) reinterpret_cast<V*>(dst + l * c_ls)[i] = r[l];
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -541,7 +500,7 @@ struct DeviceGuard {
     if (guard_.err != cudaSuccess) return cuda_fail(guard_.err, "select device")
 
 std::mutex g_mu;
-kvx_tuning g_tuning = {0, 0, 0, 0, 0};
+kvx_tuning g_tuning = {0, 0, 0, 0};
 int g_sm_count[kMaxDevices] = {0};
 bool g_bulk_attr_set[kMaxDevices][4] = {};
 
@@ -771,9 +730,6 @@ int kvx_set_tuning(const kvx_tuning* t) {
     if (t->tile_bytes < 0 || (t->tile_bytes % 16) != 0) return fail(KVX_EINVAL, "tile_bytes must be a multiple of 16");
     if (t->stages != 0 && t->stages != 4 && t->stages != 6 && t->stages != 8 && t->stages != 12)
         return fail(KVX_EINVAL, "stages must be 0, 4, 6, 8 or 12");
-    if (t->store_layer_group != 0 && t->store_layer_group != 1 && t->store_layer_group != 2 &&
-        t->store_layer_group != 4 && t->store_layer_group != 8)
-        return fail(KVX_EINVAL, "store_layer_group must be 0, 1, 2, 4 or 8");
     std::lock_guard<std::mutex> lk(g_mu);
     g_tuning = *t;
     return KVX_OK;
@@ -1409,7 +1365,6 @@ static int store_common(int32_t device, int32_t num_layers, const void* key, con
     p.num_slots = num_blocks * block_size;
     p.row_bytes = row_bytes;
     p.block_size = block_size;
-    p.num_layers = num_layers;
     p.status = status;
     const uint64_t bits = reinterpret_cast<uint64_t>(key) | reinterpret_cast<uint64_t>(value) |
                           reinterpret_cast<uint64_t>(k_cache) | reinterpret_cast<uint64_t>(v_cache) |
@@ -1428,24 +1383,8 @@ static int store_common(int32_t device, int32_t num_layers, const void* key, con
     const int64_t wpc = kStoreThreads / 32;
     const int64_t blocks = (warps + wpc - 1) / wpc;
     if (blocks > 0x7fffffff) return fail(KVX_EINVAL, "too many tokens");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int group;
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        group = g_tuning.store_layer_group;
-    }
-    if (group == 0) group = kStoreAutoLayerGroup;
-    if (num_layers > 1 && group > 1 && vec == 16) {
-        const dim3 ggrid(static_cast<unsigned>(blocks), static_cast<unsigned>((num_layers + group - 1) / group));
-        switch (group) {
-            case 2: store_kvcache_group_kernel<2><<<ggrid, kStoreThreads, 0, s>>>(p); break;
-            case 4: store_kvcache_group_kernel<4><<<ggrid, kStoreThreads, 0, s>>>(p); break;
-            default: store_kvcache_group_kernel<8><<<ggrid, kStoreThreads, 0, s>>>(p); break;
-        }
-        KVX_CUDA(cudaGetLastError(), "launch store_kvcache kernel");
-        return KVX_OK;
-    }
     const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(num_layers));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (vec) {
         case 16: store_kvcache_kernel<16><<<grid, kStoreThreads, 0, s>>>(p); break;
         case 8: store_kvcache_kernel<8><<<grid, kStoreThreads, 0, s>>>(p); break;

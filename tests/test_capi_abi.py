@@ -71,13 +71,11 @@ def test_tuning_roundtrip_and_validation(kvx_lib):
     old = _capi.Tuning()
     assert kvx_lib.kvx_get_tuning(ctypes.byref(old)) == 0
     try:
-        t = _capi.Tuning(variant=2, ctas_per_sm=1, tile_bytes=32768, stages=8, store_layer_group=2)
+        t = _capi.Tuning(variant=2, ctas_per_sm=1, tile_bytes=32768, stages=8)
         assert kvx_lib.kvx_set_tuning(ctypes.byref(t)) == 0
         back = _capi.Tuning()
         kvx_lib.kvx_get_tuning(ctypes.byref(back))
-        assert (back.variant, back.ctas_per_sm, back.tile_bytes, back.stages, back.store_layer_group) == \
-            (2, 1, 32768, 8, 2)
-        assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(store_layer_group=3))) == _capi.KVX_EINVAL
+        assert (back.variant, back.ctas_per_sm, back.tile_bytes, back.stages) == (2, 1, 32768, 8)
         assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=3))) == _capi.KVX_EINVAL
         assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(tile_bytes=100))) == _capi.KVX_EINVAL
         assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(stages=5))) == _capi.KVX_EINVAL

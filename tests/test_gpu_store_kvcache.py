@@ -87,32 +87,6 @@ def test_all_layers_in_one_launch_matches_per_layer_oracle(require_gpu):
     assert _same_bits(cache, cache_c)
 
 
-@pytest.mark.parametrize("group", [1, 2, 4, 8])
-@pytest.mark.parametrize("L", [7, 16])
-def test_all_layer_store_for_every_layer_group(require_gpu, group, L):
-    """Layers per warp of the all-layer launch, including groups that do not divide L."""
-    import ctypes
-
-    lib = require_gpu
-    old = _capi.Tuning()
-    lib.kvx_get_tuning(ctypes.byref(old))
-    lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(store_layer_group=group)))
-    try:
-        T, H, D, bs, N = 40, 8, 128, 16, 32
-        keys_c = kvgen.seeded_cache((L, T, H, D), 900 + L)
-        values_c = kvgen.seeded_cache((L, T, H, D), 901 + L)
-        cache_c = kvgen.seeded_cache((2, L, N, bs, H, D), 902 + L)
-        slots_c = kvgen.slot_mapping(T, N * bs, 903 + L)
-        keys, values, cache, slots = (t.to(DEV) for t in (keys_c, values_c, cache_c, slots_c))
-        store_kvcache_layers(keys, values, cache, slots, bs)
-        kt.check_device_status(0)
-        for layer in range(L):
-            c_oracle.store_kvcache(keys_c[layer], values_c[layer], cache_c[0, layer], cache_c[1, layer], slots_c, bs)
-        assert _same_bits(cache, cache_c)
-    finally:
-        lib.kvx_set_tuning(ctypes.byref(old))
-
-
 def test_out_of_range_slots_are_flagged_and_skipped(require_gpu):
     T, H, D, bs, N = 4, 1, 8, 2, 3
     key = torch.ones(T, H, D, device=DEV)
