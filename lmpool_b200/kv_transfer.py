@@ -593,11 +593,20 @@ def _peer_cache(ep: TransferEndpoint, peer: int) -> CacheLayout:
 
 
 def _check_registered(ep: TransferEndpoint, kv_cache, num_layers: int) -> None:
-    if ep.cache is None:
+    """The cache handed to a transfer is the one registered (and fully checked)
+    for peer mapping. O(1): the first and last layers' pointers and the block
+    stride identify it, since a registered cache is one affine allocation."""
+    reg = ep.cache
+    if reg is None:
         raise RuntimeError("no KV cache registered on this rank: call register_kv_cache before prewarm_p2p_pairs")
-    lay = affine_layout(kv_cache, num_layers)
-    if (lay.base, lay.kv_stride, lay.layer_stride, lay.block_stride, lay.num_layers) != (
-            ep.cache.base, ep.cache.kv_stride, ep.cache.layer_stride, ep.cache.block_stride, ep.cache.num_layers):
+    if num_layers != reg.num_layers:
+        raise RuntimeError(f"swap_in got num_layers={num_layers}, the registered cache has {reg.num_layers}")
+    k0, v0 = get_layer_kv(kv_cache, 0)
+    kl, vl = get_layer_kv(kv_cache, num_layers - 1)
+    last = reg.base + (num_layers - 1) * reg.layer_stride
+    e = k0.element_size()
+    if (k0.data_ptr(), v0.data_ptr(), kl.data_ptr(), vl.data_ptr(), k0.stride(0) * e, int(k0.shape[0])) != (
+            reg.base, reg.base + reg.kv_stride, last, last + reg.kv_stride, reg.block_stride, reg.num_blocks):
         raise RuntimeError("kv_cache passed to swap_in is not the cache registered for peer mapping")
 
 

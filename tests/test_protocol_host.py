@@ -69,3 +69,24 @@ def test_unknown_mode_and_unlinked_peer_are_refused():
     ep.links[1].poisoned = "earlier timeout"
     with pytest.raises(RuntimeError, match="disabled"):
         ep.exchange("push", "local", [(1, "i", 1)], [], 1.0, None)
+
+
+def test_registered_cache_check_accepts_views_and_the_tensor_and_refuses_others():
+    import torch
+
+    from lmpool_b200 import kv_transfer as kt
+    from lmpool_b200.layout import affine_layout
+
+    t = torch.empty(2, 4, 6, 8, 2, 16, dtype=torch.bfloat16)
+    ep = object.__new__(TransferEndpoint)
+    ep.cache = affine_layout(t, 4)
+    kt._check_registered(ep, t, 4)
+    kt._check_registered(ep, [(t[0, layer], t[1, layer]) for layer in range(4)], 4)
+    other = torch.empty_like(t)
+    with pytest.raises(RuntimeError, match="not the cache registered"):
+        kt._check_registered(ep, other, 4)
+    with pytest.raises(RuntimeError, match="num_layers"):
+        kt._check_registered(ep, t, 3)
+    ep.cache = None
+    with pytest.raises(RuntimeError, match="no KV cache registered"):
+        kt._check_registered(ep, t, 4)
