@@ -1,17 +1,17 @@
 #!/usr/bin/env python
 """Benchmark of LMPool's KV move path on B200 (one JSON line on rank 0).
 
-Metric (BASELINE.json): "KV move GB/s per pair (gather->NVLink->scatter,
+Metric: "KV move GB/s per pair (gather->NVLink->scatter,
 device-timed) vs blocks moved"; GB = 1e9 bytes of KV payload
 P = B * L * 2 * block_size * kv_heads * head_dim * 2 bytes moved per step
 (ModelRunner.kv_transfer_bytes, model_runner.py:808-820).
 
 Workloads (synthetic bf16 N(0,1) caches, seeded randperm block ids):
-  --gpus 1   BASELINE config 2: one GPU, Qwen3-0.6B KV geometry (L=28, H=8,
+  --gpus 1   benchmark config 2: one GPU, Qwen3-0.6B KV geometry (L=28, H=8,
              D=128, block_size=256), 2048-block cache (60 GB); a step moves
              B=512 fragmented blocks inside the cache (gather+scatter in one
              launch). The B sweep {1,4,16,64,256,512} is reported in "sweep".
-  --gpus N>1 BASELINE config 4 phase A: ranks (0,1), (2,3), ... move
+  --gpus N>1 benchmark config 4 phase A: ranks (0,1), (2,3), ... move
              B=128 blocks each way at once at Qwen3-8B geometry (L=36,
              1536-block cache per rank, 58 GB); a step is one exchange in
              the transfer mode of lmpool_b200.kv_transfer (default pull: each
@@ -221,7 +221,7 @@ def reference_gpu_local(cache: torch.Tensor, L: int, src_ids: list[int], dst_ids
 
 
 def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: int = 0) -> dict:
-    """store_kvcache at BASELINE config 5 geometry (L=80, H=8, D=128,
+    """store_kvcache at benchmark config 5 geometry (L=80, H=8, D=128,
     block_size=16, T=256 tokens per step, ~10% padding slots; the cache is
     shrunk to 4096 blocks: the cost does not depend on N). A step writes every
     layer: 80 single-layer launches as the model issues them (eager, and
@@ -443,7 +443,7 @@ def block_sums(cache: torch.Tensor, ids: list[int]) -> torch.Tensor:
 
 
 def pair_sweep(ep, link, g: dict, rank: int, stream, dist, mode: str) -> list[dict]:
-    """BASELINE config 3 on ranks 0 -> 1: B in {1, 8, 64, 256}, contiguous and
+    """benchmark config 3 on ranks 0 -> 1: B in {1, 8, 64, 256}, contiguous and
     scattered source ids. Each timed run is K back-to-back transfers in the
     configured mode, cycling through disjoint id sets so no transfer re-reads
     blocks still in L2; time = max over the two ranks."""
@@ -539,7 +539,7 @@ def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, B: int = 6
 
 
 def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: str) -> dict:
-    """BASELINE config 4 phase B: every rank sends B=32 seeded-random blocks to
+    """benchmark config 4 phase B: every rank sends B=32 seeded-random blocks to
     every other rank at once, into disjoint reserved sets; one push launch per
     rank carries all its destinations."""
     dev = torch.device("cuda", ep.device)
@@ -841,7 +841,7 @@ CONFIG5 = dict(workload="config5: 70B-like transfer (B=1024 to the NVLink partne
 
 
 def bench_config5(args) -> dict | None:
-    """BASELINE config 5 on N GPUs (pairs): the transfer alone, store_kvcache
+    """benchmark config 5 on N GPUs (pairs): the transfer alone, store_kvcache
     alone, and both at once on two streams. The cache is shrunk from 65536 to
     16384 blocks per rank (80 GiB; 65536 would be 320 GiB): transfer and store
     costs depend on B and T, not on N."""
@@ -989,7 +989,7 @@ def main() -> None:
                     help="1-GPU cache size in blocks (default: config 2's 2048); for small profiling cases")
     ap.add_argument("--blocks", type=int, default=0, help="1-GPU blocks moved per step (default 512)")
     ap.add_argument("--workload", choices=["default", "config5", "pair1p", "store"], default="default",
-                    help="config5: BASELINE config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
+                    help="config5: benchmark config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
                          "pair1p: one process, two GPUs, pair push (profiling); store: store_kvcache only")
     ap.add_argument("--pull", action="store_true", help="pair1p: destination pulls instead of source pushing")
     ap.add_argument("--pair-mode", choices=["auto", "push", "pull"], default="auto",

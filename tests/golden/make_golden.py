@@ -1,9 +1,8 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
-Run in a container that has the reference checked out (read-only) at
-``$LMPOOL_REF`` (default ``/root/reference``):
+Run where the reference is checked out (read-only), naming its root:
 
-    python tests/golden/make_golden.py
+    LMPOOL_REF=<path to the LMPool checkout> python tests/golden/make_golden.py
 
 What it records, all produced by LMPool's own code:
 
@@ -14,7 +13,7 @@ What it records, all produced by LMPool's own code:
   including repeated source ids and the list-of-layers layout.
 * ``swap_small.npz`` -- ``swap_in(..., negotiate_blocks=False)``
   (kv_transfer.py:395-475) run on two gloo CPU ranks with full arrays kept.
-* ``swap_config1.json`` -- the same call at BASELINE config 1 geometry
+* ``swap_config1.json`` -- the same call at benchmark config 1 geometry
   ([2, 28, 64, 256, 8, 128] bf16, seeds 0/1, B=8); caches are too large to
   store, so SHA-256 digests of the inputs and outputs are kept and the inputs
   are regenerated from ``tests/kvgen.py``.
@@ -35,7 +34,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("LMPOOL_REF", "/root/reference"))
+REF = Path(os.environ.get("LMPOOL_REF", "reference"))
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF / "src"))
 
@@ -206,7 +205,7 @@ def make_swaps() -> None:
     recs = run_swap("config1")
     out = {
         "description": "reference kv_transfer.swap_in(negotiate_blocks=False) on two gloo CPU ranks, "
-                       "BASELINE config 1 geometry; inputs from tests/kvgen.config1_inputs()",
+                       "benchmark config 1 geometry; inputs from tests/kvgen.config1_inputs()",
         "shape": [2, 28, 64, 256, 8, 128],
         "dtype": "bfloat16",
         "src_ids": recs[0]["src_ids"],

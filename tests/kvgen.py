@@ -2,7 +2,7 @@
 
 Every cache is i.i.d. N(0, 1) in the requested dtype drawn from
 ``torch.Generator().manual_seed(seed)`` on the CPU, and block ids come from
-``torch.randperm(N, generator=...)``, as BASELINE.json's configs specify.
+``torch.randperm(N, generator=...)``, as the benchmark configurations specify.
 The recipes are frozen: golden digests in ``tests/golden/`` depend on them.
 """
 from __future__ import annotations
@@ -23,7 +23,7 @@ def seeded_perm(n: int, seed: int) -> list[int]:
 
 
 def config1_inputs():
-    """two [2, 28, 64, 256, 8, 128] bf16 caches (seeds 0 and 1),
+    """benchmark config 1: two [2, 28, 64, 256, 8, 128] bf16 caches (seeds 0 and 1),
     8 source ids from randperm(64, seed 0), 8 destination ids from randperm(64, seed 1)."""
     shape = (2, 28, 64, 256, 8, 128)
     src = seeded_cache(shape, 0)

@@ -142,7 +142,7 @@ def test_move_within_one_cache_disjoint_ids_single_launch(variant):
 
 
 def test_config1_geometry_matches_reference_digests(variant):
-    """BASELINE config 1 data, moved on the GPU: digests equal the reference's gloo swap_in."""
+    """benchmark config 1 data, moved on the GPU: digests equal the reference's gloo swap_in."""
     rec = json.loads((GOLDEN / "swap_config1.json").read_text())
     src, dst, src_ids, dst_ids = kvgen.config1_inputs()
     src, dst = src.to(DEV), dst.to(DEV)
@@ -182,7 +182,7 @@ def test_kernel_bounds_check_flags_and_skips_bad_ids(variant):
 
 
 def test_full_config2_size_properties(variant):
-    """BASELINE config 2 at full size (L=28, N=2048, ~60 GB), B=512 fragmented ids:
+    """benchmark config 2 at full size (L=28, N=2048, ~60 GB), B=512 fragmented ids:
     moved blocks equal their sources and every other block keeps its checksum."""
     free, _ = torch.cuda.mem_get_info()
     shape = (2, 28, 2048, 256, 8, 128)

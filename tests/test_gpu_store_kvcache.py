@@ -44,7 +44,7 @@ def test_matches_reference_triton_kernel_outputs(require_gpu, case):
 
 
 def test_config5_geometry_matches_oracle(require_gpu):
-    """T=256 tokens, H=8, D=128, block_size=16, ~10% padding slots (N shrunk)."""
+    """benchmark config 5: T=256 tokens, H=8, D=128, block_size=16, ~10% padding slots (N shrunk)."""
     T, H, D, bs, N = 256, 8, 128, 16, 4096
     key_c = kvgen.seeded_cache((T, H, D), 70)
     value_c = kvgen.seeded_cache((T, H, D), 71)

@@ -93,7 +93,7 @@ def test_c_oracle_rejects_duplicate_destinations_and_bad_ids():
 
 
 def test_c_oracle_config1_matches_reference_digests():
-    """the reference's gloo swap_in digests, reproduced by the C oracle."""
+    """benchmark config 1: the reference's gloo swap_in digests, reproduced by the C oracle."""
     rec = json.loads((GOLDEN / "swap_config1.json").read_text())
     src, dst, src_ids, dst_ids = kvgen.config1_inputs()
     assert src_ids == rec["src_ids"] and dst_ids == rec["dst_ids"]
