@@ -538,35 +538,110 @@ def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, B: int = 6
             "blocks": B, "ms": ms, "GB/s": P / (ms * 1e-3) / 1e9}
 
 
-def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: str) -> dict:
-    """benchmark config 4 phase B: every rank sends B=32 seeded-random blocks to
-    every other rank at once, into disjoint reserved sets; one push launch per
-    rank carries all its destinations."""
-    dev = torch.device("cuda", ep.device)
-    N, B = g["N"], 32
+PHASE_B_BLOCKS = 32
 
-    def sets_of(r: int):
-        """(incoming targets by source, outgoing sources by destination) of rank r."""
-        others = [x for x in range(world) if x != r]
-        perm = seeded_perm(N, 5000 + r)
-        inc = {s: perm[i * B:(i + 1) * B] for i, s in enumerate(others)}
-        pool = perm[B * len(others):]
-        out = {}
-        for d in others:
-            sel = seeded_perm(len(pool), 6000 + 16 * r + d)[:B]
-            out[d] = [pool[i] for i in sel]
-        return inc, out
 
+def all_partner_sets(N: int, world: int, r: int, B: int = PHASE_B_BLOCKS):
+    """(incoming targets by source, outgoing sources by destination) of rank r
+    in benchmark config 4 phase B: seeded-random blocks, the incoming sets
+    disjoint from each other and from every outgoing set."""
+    others = [x for x in range(world) if x != r]
+    perm = seeded_perm(N, 5000 + r)
+    inc = {s: perm[i * B:(i + 1) * B] for i, s in enumerate(others)}
+    pool = perm[B * len(others):]
+    out = {}
+    for d in others:
+        sel = seeded_perm(len(pool), 6000 + 16 * r + d)[:B]
+        out[d] = [pool[i] for i in sel]
+    return inc, out
+
+
+def reference_all_partner(cache: torch.Tensor, g: dict, rank: int, world: int, dist, iters: int = 5) -> dict:
+    """Phase B with the reference's ops on the same GPUs: every rank packs each
+    destination's blocks with 2*L index_select (kv_transfer.py:463-466), all
+    payloads cross in one NCCL batch of send/recv pairs, and each received
+    payload is unpacked with 2*L index_copy_ (kv_transfer.py:468-470); wall
+    clock per step between barriers, max over ranks. Comparison leg."""
+    dev = cache.device
+    L, B = g["L"], PHASE_B_BLOCKS
     peers = [r for r in range(world) if r != rank]
-    incoming, outgoing = sets_of(rank)
-    peer_out = {s: sets_of(s)[1][rank] for s in peers}      # what each peer sends to this rank
+    incoming, outgoing = all_partner_sets(g["N"], world, rank)
+    out_idx = {d: torch.tensor(v, dtype=torch.long, device=dev) for d, v in outgoing.items()}
+    in_idx = {s: torch.tensor(v, dtype=torch.long, device=dev) for s, v in incoming.items()}
+    shape = (L, 2, B, *cache.shape[3:])
+    send = {d: torch.empty(shape, dtype=cache.dtype, device=dev) for d in peers}
+    recv = {s: torch.empty(shape, dtype=cache.dtype, device=dev) for s in peers}
+
+    def one():
+        for d in peers:
+            for layer in range(L):
+                torch.index_select(cache[0, layer], 0, out_idx[d], out=send[d][layer, 0])
+                torch.index_select(cache[1, layer], 0, out_idx[d], out=send[d][layer, 1])
+        ops = [dist.P2POp(dist.isend, send[d], d) for d in peers] + \
+              [dist.P2POp(dist.irecv, recv[s], s) for s in peers]
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+        for s in peers:
+            for layer in range(L):
+                cache[0, layer].index_copy_(0, in_idx[s], recv[s][layer, 0])
+                cache[1, layer].index_copy_(0, in_idx[s], recv[s][layer, 1])
+
+    # the kernel legs just wrote these blocks from the same sources
+    before = {s: block_sums(cache, v) for s, v in incoming.items()}
+    times = []
+    for k in range(2 + iters):
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        one()
+        torch.cuda.synchronize()
+        if k >= 2:
+            times.append((time.perf_counter() - t0) * 1e3)
+    t = torch.tensor([statistics.mean(times)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    same = all(torch.equal(before[s], block_sums(cache, v)) for s, v in incoming.items())
+    agree = [None] * world
+    dist.all_gather_object(agree, same)
+    del send, recv
+    torch.cuda.empty_cache()
+    pb = payload_bytes(g, B)
+    per_gpu_out = (world - 1) * pb / (ms * 1e-3) / 1e9
+    return {"algorithm": "index_select pack -> NCCL batched send/recv -> index_copy_ unpack",
+            "blocks_per_destination": B, "ms_per_step": ms,
+            "value": world * (world - 1) * pb / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "per_gpu_egress_GB/s": per_gpu_out, "same_blocks_as_kernel": all(agree)}
+
+
+def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: str,
+                schedule: str = "concurrent") -> dict:
+    """benchmark config 4 phase B: every rank sends B=32 seeded-random blocks to
+    every other rank, into disjoint reserved sets.
+
+    ``concurrent``: one exchange per step carries every destination and
+    source at once (one push or pull launch per rank). ``rotated``: world-1
+    exchanges per step; in exchange j rank r sends to r+j and receives from
+    r-j, so at any moment every GPU has one sender and one receiver, the
+    traffic pattern of disjoint pairs."""
+    dev = torch.device("cuda", ep.device)
+    N, B = g["N"], PHASE_B_BLOCKS
+    peers = [r for r in range(world) if r != rank]
+    incoming, outgoing = all_partner_sets(N, world, rank)
+    peer_out = {s: all_partner_sets(N, world, s)[1][rank] for s in peers}   # what each peer sends here
     in_t = {s: torch.tensor(v, dtype=torch.int64, device=dev) for s, v in incoming.items()}
     out_t = {d: torch.tensor(v, dtype=torch.int64, device=dev) for d, v in outgoing.items()}
     psrc_t = {s: torch.tensor(v, dtype=torch.int64, device=dev) for s, v in peer_out.items()}
 
-    def step():
-        ep.exchange(mode, ep.cache, [(d, out_t[d], B) for d in peers],
-                    [(s, psrc_t[s], in_t[s], B) for s in peers], 60.0, stream)
+    if schedule == "concurrent":
+        def step():
+            ep.exchange(mode, ep.cache, [(d, out_t[d], B) for d in peers],
+                        [(s, psrc_t[s], in_t[s], B) for s in peers], 60.0, stream)
+    elif schedule == "rotated":
+        def step():
+            ep.exchange_rotated(mode, ep.cache, [(d, out_t[d], B) for d in peers],
+                                [(s, psrc_t[s], in_t[s], B) for s in peers], 60.0, stream)
+    else:
+        raise ValueError(f"unknown schedule {schedule!r}")
 
     ep.status.zero_()
     for _ in range(3):
@@ -595,7 +670,7 @@ def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: s
             ok &= torch.equal(sums, gathered[d]["in"][x["rank"]])
     pb = payload_bytes(g, B)
     per_gpu_out = (world - 1) * pb / (ms * 1e-3) / 1e9
-    return {"ok": bool(ok), "blocks_per_destination": B, "ms_per_step": ms,
+    return {"ok": bool(ok), "schedule": schedule, "blocks_per_destination": B, "ms_per_step": ms,
             "value": world * (world - 1) * pb / (ms * 1e-3) / 1e9, "unit": "GB/s",
             "per_gpu_egress_GB/s": per_gpu_out, "frac_nvlink_per_gpu_egress": per_gpu_out / NVLINK_PEER_GBS,
             "verified": bool(ok)}
@@ -700,8 +775,13 @@ def bench_pairs(args) -> dict | None:
         ref_pair["this_kernel_speedup"] = ref_pair["ms"] / best
     phase_b = None
     if world >= 4:
-        phase_b = {m: all_partner(ep, cache, g, rank, world, stream, dist, m) for m in ("push", "pull")}
+        phase_b = {}
+        for sched in ("concurrent", "rotated"):
+            for m in ("push", "pull"):
+                key = m if sched == "concurrent" else f"{m}_{sched}"
+                phase_b[key] = all_partner(ep, cache, g, rank, world, stream, dist, m, sched)
         ok &= all(v["ok"] for v in phase_b.values())
+        phase_b["reference_nccl"] = reference_all_partner(cache, g, rank, world, dist)
 
     # end to end: host id lists through swap_batch (pinned H2D + status D2H per step)
     e2e_steps = max(3, min(args.steps, 30))

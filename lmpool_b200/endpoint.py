@@ -344,6 +344,30 @@ class TransferEndpoint:
         else:
             raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull' or 'push'")
 
+    def exchange_rotated(self, mode: str, local: CacheLayout, outgoing: list[tuple], incoming: list[tuple],
+                         timeout_s: float | None, stream, peer_layouts: dict | None = None) -> None:
+        """The transfers of ``exchange`` in world_size-1 rounds.
+
+        A transfer a->b belongs to round (b - a) mod world_size on both of its
+        ranks, so in round j this rank sends to rank+j and receives from
+        rank-j: every GPU has at most one sender and one receiver at a time
+        (the traffic of disjoint pairs) instead of all peers at once. Each
+        rank enqueues its rounds in increasing order and a round only waits
+        on that round's steps of its two peers, so no wait depends on a later
+        round. Every rank of a call must use this schedule.
+        """
+        if mode not in ("push", "pull"):
+            raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull' or 'push'")
+        world = self.world_size
+        rounds: dict[int, tuple[list, list]] = {}
+        for item in outgoing:
+            rounds.setdefault((item[0] - self.rank) % world, ([], []))[0].append(item)
+        for item in incoming:
+            rounds.setdefault((self.rank - item[0]) % world, ([], []))[1].append(item)
+        for j in sorted(rounds):
+            out, inc = rounds[j]
+            self.exchange(mode, local, out, inc, timeout_s, stream, peer_layouts)
+
     def read_done(self, src_rank: int) -> int:
         out = ctypes.c_uint64(0)
         _capi.check(self.lib.kvx_mailbox_read_done(self.device, ctypes.byref(self.mailbox), src_rank,

@@ -740,19 +740,32 @@ def swap_out(
 
 def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, List[int], List[int]]],
                kv_cache=None, num_layers: int | None = None, timeout_s: float | None = None,
-               stream=None, synchronize: bool = True, mode: str | None = None) -> None:
+               stream=None, synchronize: bool = True, mode: str | None = None,
+               schedule: str = "rotated") -> None:
     """Several transfers of this rank at once, in either direction.
 
     ``outgoing`` = [(dst_rank, src_block_ids)] of blocks this rank gives;
     ``incoming`` = [(src_rank, src_block_ids, local_target_block_ids)] of
-    blocks it receives. All incoming transfers share one launch and all
-    outgoing ones are only waited on, so a rank that both sends and receives
-    cannot deadlock against its peers (two sequential ``swap_in`` calls in
-    opposite directions would, with each side waiting for the other).
+    blocks it receives; each peer appears at most once in each list. The
+    exchange publishes, launches and waits in an order that cannot deadlock
+    against the peers (two sequential ``swap_in`` calls in opposite
+    directions would, with each side waiting for the other).
     ``mode`` overrides the process mode for this call; both ends of a
     transfer must use the same one. Measured on B200: pull is ~10% faster for
     one-way traffic, push ~7% faster when a pair sends both ways at once.
+    ``schedule`` orders transfers with several peers: ``"rotated"`` runs
+    them in world_size-1 rounds, round j sending to rank+j and receiving
+    from rank-j (measured on 4 B200s, all-partner exchange: 688 vs 648 GB/s
+    per GPU pushed, 640 vs 585 pulled); ``"concurrent"`` puts every peer in
+    one launch, which saves the per-round handshakes when transfers are
+    small. Every rank of the call must pass the same schedule.
     """
+    if schedule not in ("rotated", "concurrent"):
+        raise RuntimeError(f"unknown schedule {schedule!r}: expected 'rotated' or 'concurrent'")
+    for what, items in (("outgoing", outgoing), ("incoming", incoming)):
+        peers = [item[0] for item in items]
+        if len(set(peers)) != len(peers):
+            raise RuntimeError(f"swap_batch: a peer appears more than once in {what}: {peers}")
     device = _local_device(dist.get_rank())
     ep = _ENDPOINTS.get(device)
     if ep is None:
@@ -773,13 +786,19 @@ def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, 
         arrays.append(_validate(src_ids, _peer_cache(ep, src_rank).num_blocks, False, "transfer source"))
         arrays.append(_validate(dst_ids, ep.cache.num_blocks, True, "transfer destination"))
         in_spec.append((src_rank, len(arrays) - 2, len(arrays) - 1, len(dst_ids)))
+    if len(in_spec) > 1:
+        targets = np.concatenate([arrays[j] for _s, _i, j, _n in in_spec])
+        _validate(targets, ep.cache.num_blocks, True, "swap_batch targets of all incoming transfers")
     dev_ids = _upload(device, stream, *arrays) if arrays else []
     out = [(d, dev_ids[i], n) for d, i, n in out_spec]
     inc = [(s_, dev_ids[i], dev_ids[j], n) for s_, i, j, n in in_spec]
     mode = ep.mode if mode is None else mode
     with torch.cuda.stream(stream):
         ep.status.zero_()
-    ep.exchange(mode, ep.cache, out, inc, timeout_s, stream)
+    if schedule == "rotated":
+        ep.exchange_rotated(mode, ep.cache, out, inc, timeout_s, stream)
+    else:
+        ep.exchange(mode, ep.cache, out, inc, timeout_s, stream)
     if synchronize:
         ep.check_status(stream, f"swap_batch on rank {ep.rank} ({mode})",
                         peers=[o[0] for o in out] + [i[0] for i in inc])

@@ -452,6 +452,82 @@ def test_two_processes_drop_in_api_surface(require_gpu, mode):
     assert all(not r["errors"] for r in results), results
 
 
+def _all_partner_worker(rank: int, world: int, port: int, queue, mode: str, schedule: str) -> None:
+    """Every rank gives blocks to every other rank in one swap_batch call;
+    each rank checks its whole cache against the oracle's model of all ranks."""
+    import torch.distributed as dist
+
+    from lmpool_b200 import kv_transfer as kt
+
+    try:
+        torch.cuda.set_device(rank)
+        os.environ["LOCAL_RANK"] = str(rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", world_size=world, rank=rank)
+        N, B = 48, 3
+        shape = (2, 4, N, 16, 2, 64)
+        model = [kvgen.seeded_cache(shape, 600 + r) for r in range(world)]
+        cache = model[rank].to(f"cuda:{rank}")
+        kt.register_kv_cache(cache, 4)
+        pairs = [(a, b) for a in range(world) for b in range(a + 1, world)]
+        kt.prewarm_p2p_pairs(pairs, num_layers=4, block_size=16, num_kv_heads=2, head_dim=64, num_blocks=2,
+                             dtype=torch.bfloat16, timeout_s=20)
+        errors = []
+        for call in range(2):
+            # per rank: targets for each source first, then a pool the sources come from
+            perms = [kvgen.seeded_perm(N, 610 + 10 * call + r) for r in range(world)]
+            targets = {(a, b): perms[b][a * B:(a + 1) * B] for a in range(world) for b in range(world) if a != b}
+            sources = {(a, b): perms[a][world * B + b * B:world * B + (b + 1) * B]
+                       for a in range(world) for b in range(world) if a != b}
+            peers = [x for x in range(world) if x != rank]
+            kt.swap_batch([(d, sources[(rank, d)]) for d in peers],
+                          [(s_, sources[(s_, rank)], targets[(s_, rank)]) for s_ in peers],
+                          timeout_s=20, mode=mode, schedule=schedule)
+            new = [m.clone() for m in model]
+            for (a, b), src_ids in sources.items():
+                c_oracle.swap_planned(model[a], src_ids, new[b], targets[(a, b)], nthreads=2)
+            model = new
+            dist.barrier()
+            if not _same_bits(cache, model[rank]):
+                errors.append(f"cache of rank {rank} differs after call {call}")
+        kt.shutdown()
+        queue.put({"rank": rank, "errors": errors})
+        dist.destroy_process_group()
+    except Exception as exc:  # noqa: BLE001
+        queue.put({"rank": rank, "errors": [repr(exc)]})
+        raise
+
+
+@pytest.mark.skipif(device_count() < 3, reason="needs 3 GPUs")
+@pytest.mark.parametrize("schedule", ["rotated", "concurrent"])
+@pytest.mark.parametrize("mode", ["pull", "push"])
+def test_all_partner_swap_batch_matches_oracle(require_gpu, mode, schedule):
+    world = min(device_count(), 4)
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_all_partner_worker, args=(r, world, port, queue, mode, schedule))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    deadline = time.time() + 300
+    try:
+        while len(results) < world and time.time() < deadline:
+            try:
+                results.append(queue.get(timeout=1))
+            except Exception:  # noqa: BLE001 - queue.Empty
+                if any(p.exitcode not in (None, 0) for p in procs):
+                    break
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+    assert len(results) == world, results
+    assert all(not r["errors"] for r in results), results
+
+
 # -- destination-driven (pull) mode ------------------------------------------------
 
 @pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])

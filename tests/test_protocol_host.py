@@ -90,3 +90,98 @@ def test_registered_cache_check_accepts_views_and_the_tensor_and_refuses_others(
     ep.cache = None
     with pytest.raises(RuntimeError, match="no KV cache registered"):
         kt._check_registered(ep, t, 4)
+
+
+def test_rotated_schedule_puts_each_transfer_in_round_peer_offset():
+    ep, calls = _endpoint(1, 4)
+    ep.exchange_rotated("push", "local", [(2, "i2", 5), (0, "i0", 6)], [(3, "s3", "d3", 7), (0, "s0", "d0", 8)],
+                        1.0, None)
+    # round j sends to rank+j and receives from rank-j (mod 4): j=1 out 2 and in 0, j=2 in 3, j=3 out 0
+    pushes = [c[1] for c in calls if c[0] == "push"]
+    publishes = [(c[1], c[2]) for c in calls if c[0] == "publish"]
+    assert pushes == [[(2, "cache2", 5)], [(0, "cache0", 6)]]
+    assert publishes == [(0, 8), (3, 7)]
+    kinds = [c[0] for c in calls]
+    assert kinds == ["publish", "wait_armed", "push", "wait_done",   # round 1
+                     "publish", "wait_done",                         # round 2
+                     "wait_armed", "push"]                           # round 3
+    with pytest.raises(RuntimeError, match="mode"):
+        ep.exchange_rotated("sideways", "local", [], [], 1.0, None)
+
+
+def _simulate(streams: dict[int, list], mode: str) -> None:
+    """Run every rank's recorded device steps against one another, in any
+    interleaving, with the mailbox semantics of the kernels: an arm slot per
+    (source, destination) that must be free when published, a done token the
+    destination waits for, a pulled report the source waits for. Raises on a
+    deadlock (no rank can make progress) or a clobbered mailbox."""
+    arm, done, pulled = {}, {}, {}
+    pos = {r: 0 for r in streams}
+    while any(pos[r] < len(streams[r]) for r in streams):
+        progressed = False
+        for r, steps in streams.items():
+            while pos[r] < len(steps):
+                step = steps[pos[r]]
+                kind = step[0]
+                if kind == "publish":                 # r is the destination, step[1] the source
+                    assert (step[1], r) not in arm, "arm published twice before the source used it"
+                    arm[(step[1], r)] = step[3]
+                elif kind == "wait_armed":
+                    if (r, step[1]) not in arm:
+                        break
+                elif kind == "push":
+                    for peer, _layout, _n in step[1]:
+                        done[(r, peer)] = arm.pop((r, peer))
+                elif kind == "wait_done":
+                    if done.get((step[1], r)) != step[2]:
+                        break
+                    del done[(step[1], r)]
+                elif kind == "pull":
+                    for peer, _layout, _n, _token in step[1]:
+                        pulled[(peer, r)] = pulled.get((peer, r), 0) + 1
+                elif kind == "wait_pulled":
+                    if not pulled.get((r, step[1])):
+                        break
+                    pulled[(r, step[1])] -= 1
+                pos[r] += 1
+                progressed = True
+        if not progressed:
+            raise AssertionError(f"deadlock ({mode}): " + ", ".join(
+                f"rank {r} stuck at {streams[r][pos[r]]}" for r in streams if pos[r] < len(streams[r])))
+    assert not arm and not done and not any(pulled.values())
+
+
+@pytest.mark.parametrize("mode", ["push", "pull"])
+@pytest.mark.parametrize("schedule", ["concurrent", "rotated"])
+@pytest.mark.parametrize("world,seed", [(2, 0), (4, 1), (6, 2), (8, 3), (8, 4)])
+def test_every_rank_finishes_for_random_transfer_sets(mode, schedule, world, seed):
+    """Any set of directed transfers, each rank calling the same schedule
+    several times in a row, completes without a deadlock."""
+    import random
+
+    rng = random.Random(seed)
+    streams = {}
+    eps = {r: _endpoint(r, world) for r in range(world)}
+    for _call in range(3):
+        pairs = {(a, b) for a in range(world) for b in range(world) if a != b and rng.random() < 0.6}
+        for r, (ep, _calls) in eps.items():
+            outgoing = [(b, f"i{b}", 1 + rng.randrange(4)) for a, b in sorted(pairs) if a == r]
+            incoming = [(a, f"s{a}", f"d{a}", 1) for a, b in sorted(pairs) if b == r]
+            getattr(ep, "exchange" if schedule == "concurrent" else "exchange_rotated")(
+                mode, "local", outgoing, incoming, 1.0, None)
+    for r, (_ep, calls) in eps.items():
+        streams[r] = calls
+    _simulate(streams, mode)
+
+
+def test_simulator_detects_a_deadlock():
+    """Two sequential one-way calls in opposite directions, push mode: each
+    rank first waits for the other's arm."""
+    a, ca = _endpoint(0, 2)
+    b, cb = _endpoint(1, 2)
+    a.exchange("push", "local", [(1, "i", 1)], [], 1.0, None)
+    a.exchange("push", "local", [], [(1, "s", "d", 1)], 1.0, None)
+    b.exchange("push", "local", [(0, "i", 1)], [], 1.0, None)
+    b.exchange("push", "local", [], [(0, "s", "d", 1)], 1.0, None)
+    with pytest.raises(AssertionError, match="deadlock"):
+        _simulate({0: ca, 1: cb}, "push")
