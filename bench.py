@@ -58,6 +58,24 @@ CPU_SAMPLE_BLOCKS = 16
 L2_FLUSH_BYTES = 512 << 20
 
 
+class L2Flush:
+    """Evicts L2 between timed launches: writes a buffer larger than L2, then
+    reads another one, so the timed launch finds neither its own data nor
+    dirty lines of the flush (whose write-back would otherwise be charged to
+    it: +2 to +8 us per launch at 1-4 blocks, measured). ``dirty=True``
+    skips the read, for the write-only figure."""
+
+    def __init__(self, dev):
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self, dirty: bool = False) -> None:
+        self.w.zero_()
+        if not dirty:
+            torch.sum(self.r, dim=0, out=self.sink)
+
+
 def payload_bytes(g: dict, blocks: int) -> int:
     return blocks * g["L"] * 2 * g["bs"] * g["H"] * g["D"] * 2
 
@@ -226,7 +244,8 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: 
     shrunk to 4096 blocks: the cost does not depend on N). A step writes every
     layer: 80 single-layer launches as the model issues them (eager, and
     captured in a CUDA graph as the decode path does), or one all-layer
-    launch. L2 is flushed between timed steps."""
+    launch. L2 is flushed (written, then another buffer read) between timed
+    steps."""
     from lmpool_b200.attention import store_kvcache, store_kvcache_layers
     from lmpool_b200.kv_transfer import check_device_status
 
@@ -244,7 +263,7 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: 
     valid = int((slots >= 0).sum())
     slots = slots.to(dev)
     stream = torch.cuda.current_stream(dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
 
     def per_layer():
         for layer in range(c["L"]):
@@ -266,7 +285,7 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: 
             fn()
         times = []
         for _ in range(iters):
-            flush.zero_()
+            flush()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             fn()
@@ -355,8 +374,8 @@ def bench_local(args) -> dict:
                           "hbm_GB/s": achieved, "frac": achieved / peak}), flush=True)
         return None
 
-    # B sweep, L2 flushed before each timed launch
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    # B sweep, L2 flushed before each timed launch (clean, and write-only)
+    flush = L2Flush(dev)
     sweep = []
     for b in SWEEP_B:
         s_t, d_t = ids_for(b)
@@ -364,18 +383,22 @@ def bench_local(args) -> dict:
         for _ in range(3):
             kt._launch_move(dev_idx, lay, lay, s_t, d_t, b, status, stream)
         iters = 30 if b <= 64 else 10
-        times = []
-        for _ in range(iters):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            kt._launch_move(dev_idx, lay, lay, s_t, d_t, b, status, stream)
-            e1.record(stream)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-        t = statistics.median(times) * 1e-3
+        med = {}
+        for dirty in (False, True):
+            times = []
+            for _ in range(iters):
+                flush(dirty)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                kt._launch_move(dev_idx, lay, lay, s_t, d_t, b, status, stream)
+                e1.record(stream)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            med[dirty] = statistics.median(times) * 1e-3
+        t = med[False]
         sweep.append({"blocks": b, "bytes": pb, "ms": t * 1e3, "GB/s": pb / t / 1e9,
-                      "hbm_GB/s": 2 * pb / t / 1e9, "frac_hbm": 2 * pb / t / 1e9 / peak})
+                      "hbm_GB/s": 2 * pb / t / 1e9, "frac_hbm": 2 * pb / t / 1e9 / peak,
+                      "ms_dirty_l2": med[True] * 1e3, "frac_hbm_dirty_l2": 2 * pb / med[True] / 1e9 / peak})
     del flush
 
     # end to end through the public API: host id lists -> pinned -> device,
@@ -408,7 +431,8 @@ def bench_local(args) -> dict:
         "config": {"workload": g["workload"], "num_layers": g["L"], "num_blocks": g["N"], "block_size": g["bs"],
                    "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_moved": B, "payload_bytes_per_step": P,
                    "src_ids": "randperm[:512]", "dst_ids": "randperm[512:1024]",
-                   "l2": "inputs larger than L2 (15 GB read + 15 GB written per step); sweep flushes L2",
+                   "l2": "inputs larger than L2 (15 GB read + 15 GB written per step); the sweep flushes L2 "
+                         "before each launch by writing 512 MB then reading 512 MB (ms_dirty_l2: write only)",
                    "parallelism": "replicas only"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_src,
