@@ -186,9 +186,12 @@ def build_metadata(args) -> dict:
     dtype = _DTYPES[args.resolved_dtype]
     names = [torch.cuda.get_device_name(i) for i in range(min(2, torch.cuda.device_count()))] \
         if torch.cuda.is_available() else []
+    from .kv_transfer import transfer_mode
+
     return {
         "benchmark": "benchmark_kv_transfer",
-        "implementation": "lmpool_b200 NVLink push (CUDA IPC), sm_100a",
+        "implementation": f"lmpool_b200 NVLink {transfer_mode()} (CUDA IPC), sm_100a",
+        "transfer_mode": transfer_mode(),
         "model": {"label": args.model_label or f"custom-{args.resolved_dtype}"},
         "resolved_config": {
             "num_layers": args.num_layers,

@@ -31,6 +31,7 @@ def test_metadata_has_what_the_profile_builder_reads():
         assert key in rc
     assert rc["num_layers"] == 36 and rc["torch_dtype"] == "bfloat16" and rc["kv_dtype_bytes"] == 2
     assert meta["model"]["label"]
+    assert meta["transfer_mode"] in ("pull", "push") and meta["transfer_mode"] in meta["implementation"]
     json.dumps(meta)
 
 
