@@ -214,8 +214,9 @@ int kvx_pair_wait_pulled(int32_t device, const kvx_mailbox* my_mailbox, int32_t 
  *
  * Some callers cannot call cudaMalloc: a serving process whose memory is
  * already handed out (LMPool sizes its KV cache to take the configured share
- * of all free GPU memory), code that runs while a CUDA graph is being
- * captured, or a host whose own allocator owns every byte of device memory.
+ * of all free GPU memory), a plugin whose host program forbids it to
+ * allocate device memory, or a host whose own allocator owns every byte of
+ * device memory.
  * kvx_pair_push keeps its scratch -- one CTA-completion counter per
  * destination rank -- in the mailbox region, which kvx_mailbox_create
  * allocates with cudaMalloc. This variant moves the same bytes with the same

@@ -2,9 +2,9 @@
 
 Some callers of this library cannot allocate device memory: a serving process
 whose GPU memory is already taken (LMPool gives its KV cache the configured
-share of all free memory), code running during CUDA graph capture, or a host
-whose own allocator owns all device memory. The allocation-free push keeps
-the kernel's scratch (per-destination CTA-completion counters) in a fixed
+share of all free memory), a plugin whose host program forbids it to allocate
+device memory, or a host whose own allocator owns all device memory. The
+allocation-free push keeps the kernel's scratch (per-destination CTA-completion counters) in a fixed
 array inside the library, so such a caller needs nothing allocated for it.
 
 This test calls it through the C ABI and checks its output against the
