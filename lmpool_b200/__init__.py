@@ -8,9 +8,12 @@ Modules:
                 kv_transfer_bytes)
   endpoint      per-GPU mailbox, peer mappings, pair protocol
   layout        KV-cache layouts -> byte descriptors
+  topology      NVLink pair detection (drop-in for the nvidia-smi parser)
+  benchmark_kv_transfer  LMPool's pair microbenchmark through this package
+  latency_profiles/      B200 transfer-latency profiles for LMPool's admission
   _capi         ctypes binding of include/kvx.h (library _kvx.so)
   _build        nvcc recipe for _kvx.so
 """
 
-__all__ = ["kv_transfer", "attention", "model_runner", "endpoint", "layout"]
+__all__ = ["kv_transfer", "attention", "model_runner", "endpoint", "layout", "topology"]
 __version__ = "0.1.0"
