@@ -185,3 +185,47 @@ def test_simulator_detects_a_deadlock():
     b.exchange("push", "local", [], [(0, "s", "d", 1)], 1.0, None)
     with pytest.raises(AssertionError, match="deadlock"):
         _simulate({0: ca, 1: cb}, "push")
+
+
+def _batch_setup(monkeypatch):
+    """swap_batch up to its first device step: a registered CPU-shaped cache
+    on a stub endpoint, peers 1-3 linked with caches of the same shape."""
+    import torch
+
+    from lmpool_b200 import kv_transfer as kt
+    from lmpool_b200.layout import affine_layout
+
+    lay = affine_layout(torch.empty(2, 2, 10, 4, 1, 8, dtype=torch.bfloat16), 2)
+    ep, calls = _endpoint(0, 4)
+    ep.cache = lay
+    for link in ep.links.values():
+        link.cache = lay
+    monkeypatch.setattr(kt.dist, "get_rank", lambda: 0)
+    monkeypatch.setattr(kt, "_local_device", lambda rank: 0)
+    monkeypatch.setitem(kt._ENDPOINTS, 0, ep)
+
+    def no_upload(*a, **k):
+        raise AssertionError("reached the device upload")
+
+    monkeypatch.setattr(kt, "_upload", no_upload)
+    return kt, calls
+
+
+def test_swap_batch_refuses_bad_batches_before_any_device_step(monkeypatch):
+    kt, calls = _batch_setup(monkeypatch)
+    S = "stream"   # no CUDA here: stands in for the caller's stream
+    with pytest.raises(RuntimeError, match="more than once in outgoing"):
+        kt.swap_batch([(1, [0]), (1, [2])], [])
+    with pytest.raises(RuntimeError, match="more than once in incoming"):
+        kt.swap_batch([], [(2, [0], [1]), (2, [3], [4])])
+    with pytest.raises(RuntimeError, match="schedule"):
+        kt.swap_batch([(1, [0])], [], schedule="sideways")
+    with pytest.raises(RuntimeError, match="targets of all incoming"):
+        kt.swap_batch([], [(1, [0, 1], [5, 6]), (3, [2], [6])], stream=S)   # block 6 written by two sources
+    with pytest.raises(RuntimeError, match="3 source ids, 2 targets"):
+        kt.swap_batch([], [(1, [0, 1, 2], [5, 6])], stream=S)
+    with pytest.raises(RuntimeError, match="outside"):
+        kt.swap_batch([(2, [10])], [], stream=S)
+    assert calls == []
+    with pytest.raises(AssertionError, match="device upload"):     # a good batch gets that far
+        kt.swap_batch([(1, [0, 1])], [(1, [2], [7]), (3, [2], [8])], stream=S)
