@@ -107,8 +107,12 @@ class TransferEndpoint:
         self.tokens_issued: dict[int, int] = {}
         self._lock = threading.Lock()
         self._ipc_maps: dict[bytes, list] = {}   # handle -> [base address, references]
-        # word 0: this endpoint's per-call status (zeroed per transfer)
+        # word 0: this endpoint's per-call status (zeroed per transfer); read
+        # back through a pinned word, one copy and one stream sync per check
         self.status = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", self.device))
+        self.status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._status_host_np = self.status_host.numpy()
+        self.status_clean = True    # the device word is zero and nothing enqueued since
         self.mode = "pull"          # pair transfer mode used by exchange(); the same on every rank
         self.closed = False
 
@@ -315,6 +319,7 @@ class TransferEndpoint:
         read this rank's blocks. Either order leaves no wait depending on a
         later launch of any rank.
         """
+        self.status_clean = False
         layouts = peer_layouts or {}
         if mode == "push":
             tokens = []
@@ -374,10 +379,24 @@ class TransferEndpoint:
                                                    ctypes.byref(out)), "kvx_mailbox_read_done")
         return out.value
 
+    def reset_status(self, stream) -> None:
+        """Zero the status word on ``stream`` before a transfer, unless the
+        last check read zero and nothing has been enqueued since."""
+        if not self.status_clean:
+            with torch.cuda.stream(stream):
+                self.status.zero_()
+
     def check_status(self, stream, what: str, peers=()) -> None:
+        if stream == torch.cuda.current_stream(self.device):
+            self.status_host.copy_(self.status, non_blocking=True)
+        else:
+            with torch.cuda.stream(stream):
+                self.status_host.copy_(self.status, non_blocking=True)
         stream.synchronize()
-        bits = int(self.status.item())
-        if bits:
+        bits = int(self._status_host_np[0])
+        if not bits:
+            self.status_clean = True
+        else:
             if bits & (_capi.DEV_TIMEOUT | _capi.DEV_PIPE_TIMEOUT):
                 # A peer that is merely late may still write into blocks this
                 # rank is about to give back; refuse further use of the pair.

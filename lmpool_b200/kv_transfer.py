@@ -168,8 +168,9 @@ class _IdStager:
             with torch.cuda.stream(stream):
                 out = torch.empty(total, dtype=torch.int64, device=dev)
                 out.copy_(self.pinned[:total], non_blocking=True)
+            if self.event is None:
                 self.event = torch.cuda.Event()
-                self.event.record(stream)
+            self.event.record(stream)
         views, off = [], 0
         for a in arrays:
             views.append(out[off:off + a.size])
@@ -559,8 +560,7 @@ def prewarm_p2p_pairs(
 
 def _run_exchange(ep: TransferEndpoint, local: CacheLayout, outgoing: list, incoming: list,
                   timeout_s: float | None, stream, peer_layouts: dict | None, what: str) -> None:
-    with torch.cuda.stream(stream):
-        ep.status.zero_()
+    ep.reset_status(stream)
     ep.exchange(ep.mode, local, outgoing, incoming, timeout_s, stream, peer_layouts)
     peers = [o[0] for o in outgoing] + [i[0] for i in incoming]
     ep.check_status(stream, what, peers=peers)
@@ -578,8 +578,10 @@ def _destination_side(ep: TransferEndpoint, src_rank: int, src_ids: List[int], d
 
 def _source_side(ep: TransferEndpoint, dst_rank: int, src_ids: List[int], timeout_s: float | None, stream,
                  local: CacheLayout | None = None, remote: CacheLayout | None = None) -> None:
-    """Give ``src_ids`` to ``dst_rank`` (blocks until the destination holds them)."""
-    (sids,) = _upload(ep.device, stream, _id_array(src_ids))
+    """Give ``src_ids`` to ``dst_rank`` (blocks until the destination holds them).
+    In pull mode the destination reads the ids it was given itself, so the
+    source uploads none."""
+    sids = None if ep.mode == "pull" else _upload(ep.device, stream, _id_array(src_ids))[0]
     layouts = {dst_rank: remote} if remote is not None else None
     _run_exchange(ep, ep.cache if local is None else local, [(dst_rank, sids, len(src_ids))], [], timeout_s,
                   stream, layouts, f"transfer {ep.rank}->{dst_rank} (source, {ep.mode})")
@@ -793,8 +795,7 @@ def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, 
     out = [(d, dev_ids[i], n) for d, i, n in out_spec]
     inc = [(s_, dev_ids[i], dev_ids[j], n) for s_, i, j, n in in_spec]
     mode = ep.mode if mode is None else mode
-    with torch.cuda.stream(stream):
-        ep.status.zero_()
+    ep.reset_status(stream)
     if schedule == "rotated":
         ep.exchange_rotated(mode, ep.cache, out, inc, timeout_s, stream)
     else:
