@@ -242,18 +242,21 @@ class TransferEndpoint:
 
     # -- protocol steps (enqueue only) ----------------------------------------
     def publish(self, link: PeerLink, dst_ids: torch.Tensor, num_ids: int, token: int, stream) -> None:
+        self.status_clean = False
         _capi.check(self.lib.kvx_pair_publish(self.device, ctypes.byref(link.mailbox), self.rank,
                                               ctypes.c_void_p(dst_ids.data_ptr() if num_ids else 0), num_ids, token,
                                               ctypes.c_void_p(_capi.stream_handle(stream))),
                     "kvx_pair_publish")
 
     def wait_done(self, src_rank: int, token: int, timeout_s: float | None, stream) -> None:
+        self.status_clean = False
         _capi.check(self.lib.kvx_pair_wait_done(self.device, ctypes.byref(self.mailbox), src_rank, token,
                                                 timeout_ns(timeout_s), ctypes.c_void_p(self.status.data_ptr()),
                                                 ctypes.c_void_p(_capi.stream_handle(stream))),
                     "kvx_pair_wait_done")
 
     def wait_armed(self, link: PeerLink, num_ids: int, timeout_s: float | None, stream) -> None:
+        self.status_clean = False
         _capi.check(self.lib.kvx_pair_wait_armed(self.device, ctypes.byref(self.mailbox), ctypes.byref(link.mailbox),
                                                  self.rank, link.peer, num_ids, timeout_ns(timeout_s),
                                                  ctypes.c_void_p(self.status.data_ptr()),
@@ -262,6 +265,7 @@ class TransferEndpoint:
 
     def push(self, src: CacheLayout, targets: list[tuple[PeerLink, CacheLayout, torch.Tensor, int]], stream) -> None:
         """One launch per group of up to 8 targets: (link, peer layout, src ids, count)."""
+        self.status_clean = False
         for start in range(0, len(targets), MAX_TARGETS_PER_LAUNCH):
             group = targets[start:start + MAX_TARGETS_PER_LAUNCH]
             arr = (_capi.PushTarget * len(group))()
@@ -281,6 +285,7 @@ class TransferEndpoint:
     def pull(self, local: CacheLayout, sources: list[tuple], stream) -> None:
         """Destination-driven copy: one launch per group of up to 8 sources,
         each (link, peer layout, src ids, dst ids, count, token)."""
+        self.status_clean = False
         dst_desc = local.desc()
         for start in range(0, len(sources), MAX_TARGETS_PER_LAUNCH):
             group = sources[start:start + MAX_TARGETS_PER_LAUNCH]
@@ -300,6 +305,7 @@ class TransferEndpoint:
                         "kvx_pair_pull")
 
     def wait_pulled(self, dst_rank: int, timeout_s: float | None, stream) -> None:
+        self.status_clean = False
         _capi.check(self.lib.kvx_pair_wait_pulled(self.device, ctypes.byref(self.mailbox), dst_rank,
                                                   timeout_ns(timeout_s), ctypes.c_void_p(self.status.data_ptr()),
                                                   ctypes.c_void_p(_capi.stream_handle(stream))),

@@ -229,3 +229,36 @@ def test_swap_batch_refuses_bad_batches_before_any_device_step(monkeypatch):
     assert calls == []
     with pytest.raises(AssertionError, match="device upload"):     # a good batch gets that far
         kt.swap_batch([(1, [0, 1])], [(1, [2], [7]), (3, [2], [8])], stream=S)
+
+
+def test_every_enqueued_step_marks_the_status_word_unchecked():
+    """reset_status skips the zeroing launch only while the last check read
+    zero and nothing was enqueued since; every device step clears that."""
+    import torch
+
+    from lmpool_b200 import _capi
+    from lmpool_b200.layout import affine_layout
+
+    class Lib:
+        def __getattr__(self, name):
+            return lambda *args: 0
+
+    lay = affine_layout(torch.empty(2, 1, 4, 2, 1, 8, dtype=torch.bfloat16), 1)
+    ep = object.__new__(TransferEndpoint)
+    ep.lib, ep.device, ep.rank = Lib(), 0, 0
+    ep.mailbox = _capi.Mailbox()
+    ep.status = torch.zeros(1, dtype=torch.int32)
+    link = PeerLink(peer=1, mailbox=_capi.Mailbox(), cache=lay)
+    ids = torch.zeros(2, dtype=torch.int64)
+    steps = [
+        lambda: ep.publish(link, ids, 2, 1, None),
+        lambda: ep.wait_done(1, 1, 1.0, None),
+        lambda: ep.wait_armed(link, 2, 1.0, None),
+        lambda: ep.push(lay, [(link, lay, ids, 2)], None),
+        lambda: ep.pull(lay, [(link, lay, ids, ids, 2, 1)], None),
+        lambda: ep.wait_pulled(1, 1.0, None),
+    ]
+    for step in steps:
+        ep.status_clean = True
+        step()
+        assert ep.status_clean is False
