@@ -8,9 +8,12 @@
  *   -------------------------------------------------  ------------------------------
  *   kv_transfer.py:229-248 _pack_all_layer_blocks      kvx_move_blocks (dst = payload)
  *   kv_transfer.py:264-276 _unpack_all_layer_blocks    kvx_move_blocks (src = payload)
- *   kv_transfer.py:395-475 swap_in (planned path,      kvx_pair_publish + kvx_pair_wait_done
- *     negotiate_blocks=False): index_select ->           (destination), kvx_pair_wait_armed +
- *     NCCL send/recv -> index_copy_                      kvx_pair_push (source)
+ *   kv_transfer.py:395-475 swap_in (planned path,      pull (default): kvx_pair_pull
+ *     negotiate_blocks=False): index_select ->           (destination), kvx_pair_wait_pulled
+ *     NCCL send/recv -> index_copy_                      (source); push: kvx_pair_publish +
+ *                                                        kvx_pair_wait_done (destination),
+ *                                                        kvx_pair_wait_armed + kvx_pair_push
+ *                                                        (source)
  *   kv_transfer.py:40-119 prewarm_p2p_pairs            kvx_ipc_export / kvx_ipc_open /
  *     (pair NCCL communicators)                          kvx_mailbox_create
  *   layers/attention.py:7-108 store_kvcache            kvx_store_kvcache,
