@@ -14,17 +14,23 @@ Workloads (synthetic bf16 N(0,1) caches, seeded randperm block ids):
   --gpus N>1 benchmark config 4 phase A: ranks (0,1), (2,3), ... move
              B=128 blocks each way at once at Qwen3-8B geometry (L=36,
              1536-block cache per rank, 58 GB); a step is one exchange in
-             the transfer mode of lmpool_b200.kv_transfer (default pull: each
-             rank bulk-loads its partner's blocks over NVLink, then waits for
-             the partner's report; push: arm, push, completion wait).
-  --impl reference  the reference algorithm on the host cores (C oracle:
-             pack into a payload, then unpack; rank 0 only), same geometry.
+             push mode (arm, push, completion wait). The line adds config 3
+             (N=2), config 4 phase B (N>=4) and config 5, each verified.
+  --impl reference  the reference's CPU path on the host cores (rank 0 only):
+             pack + unpack with torch ops in one process (N=1), or two gloo
+             ranks exchanging one pair's blocks both ways (N>1).
 
 Timing: W untimed warm-up steps, then K steps between a barrier and a
 device synchronisation, CUDA events on the launching stream, max over ranks.
 Every step's inputs exceed the 126 MB L2 (config 2: 15 GB read + 15 GB
 written per step; config 4: 4.8 GB per direction), so no flush is needed for
-the headline; the sweep flushes L2 before each timed launch.
+the headline; the sweeps flush L2 before each timed launch.
+
+Verification: every moved block is compared byte for byte -- with its
+source (1 GPU), or with the bytes the reference's own algorithm delivers on
+the same GPUs (index_select -> NCCL send/recv, per plane and layer) -- and
+every other block is checked unchanged through a 64-bit per-block
+fingerprint taken before and after.
 """
 from __future__ import annotations
 
@@ -51,11 +57,20 @@ LOCAL = dict(workload="config2: 1-GPU local gather+scatter, Qwen3-0.6B KV geomet
              D=128, B=512)
 PAIRS = dict(workload="config4 phase A: disjoint NVLink pairs, both directions at once, Qwen3-8B KV geometry", L=36,
              N=1536, bs=256, H=8, D=128, B=128)
+CONFIG5 = dict(workload="config5: 70B-like transfer (B=1024 to the NVLink partner, both directions) under "
+                        "concurrent store_kvcache (T=256 tokens x 80 layers per step)",
+               L=80, N=16384, bs=16, H=8, D=128, B=1024, T=256)
+STORE = dict(L=80, H=8, D=128, bs=16, N=4096, T=256)
 SWEEP_B = [1, 4, 16, 64, 256, 512]
-NVLINK_PEER_GBS = 770.0     # measured peer copy per direction on this pool (profiling recipe)
+PAIR_SWEEP_B = [1, 8, 64, 256]
+PHASE_B_BLOCKS = 32
+# Per-direction NVLink 5 bandwidth of one B200 (900 GB/s nominal): the pair
+# roofline. A plain peer copy is measured in the same run for comparison.
+NVLINK_NOMINAL_GBS = 900.0
 FALLBACK_HBM_GBS = 6650.0
 CPU_SAMPLE_BLOCKS = 16
 L2_FLUSH_BYTES = 512 << 20
+FP_MULT = -7046029254386353131   # odd 64-bit constant (as a signed int64) folding planes and layers
 
 
 class L2Flush:
@@ -89,18 +104,36 @@ def hbm_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback (profiling recipe, 6.65 TB/s)"
 
 
-def profile_traffic(name: str) -> float | None:
-    """dram bytes per launch recorded in a committed ncu summary (profiles/<name>.txt)."""
+def profile_value(name: str, key: str) -> float | None:
+    """A ``key: value`` figure recorded in a committed ncu summary (profiles/<name>.txt)."""
     p = ROOT / "profiles" / f"{name}.txt"
     if not p.exists():
         return None
-    m = re.search(r"^dram_bytes_per_launch_full_size:\s*([0-9.eE+]+)", p.read_text(), re.M)
+    m = re.search(rf"^{re.escape(key)}:\s*([0-9.eE+]+)", p.read_text(), re.M)
     return float(m.group(1)) if m else None
 
 
 def seeded_perm(n: int, seed: int) -> list[int]:
     g = torch.Generator().manual_seed(int(seed))
     return torch.randperm(int(n), generator=g).tolist()
+
+
+def line_config(g: dict, world: int) -> dict:
+    """The ``config`` object of the JSON line; both arms print the same one."""
+    cfg = {"workload": g["workload"], "num_layers": g["L"], "num_blocks": g["N"], "block_size": g["bs"],
+           "num_kv_heads": g["H"], "head_dim": g["D"], "dtype": "bf16"}
+    if world <= 1:
+        cfg.update({"blocks_moved": g["B"], "payload_bytes_per_step": payload_bytes(g, g["B"]),
+                    "src_ids": "randperm[:512]", "dst_ids": "randperm[512:1024]",
+                    "l2": "inputs larger than L2 (15 GB read + 15 GB written per step); the sweep flushes L2 "
+                          "before each launch by writing 512 MB then reading 512 MB (ms_dirty_l2: write only)",
+                    "parallelism": "replicas only"})
+    else:
+        cfg.update({"blocks_moved_per_direction": g["B"], "payload_bytes_per_rank_per_step": payload_bytes(g, g["B"]),
+                    "pairs": [(r, r + 1) for r in range(0, world, 2)],
+                    "l2": "inputs larger than L2 (4.8 GB per direction per step)",
+                    "parallelism": f"{world // 2} NVLink pairs over CUDA IPC, no collective on the data path"})
+    return cfg
 
 
 class ClockSampler:
@@ -159,20 +192,98 @@ class ClockSampler:
 
 def merge_clocks(items: list[dict]) -> dict:
     sms = [c["sm_mhz"] for c in items if c.get("sm_mhz")]
-    out = {"sm_mhz": statistics.median(sms) if sms else None,
-           "sm_max_mhz": max((c["sm_max_mhz"] for c in items if c.get("sm_max_mhz")), default=None),
-           "reasons": sorted({r for c in items for r in c.get("reasons", [])}),
-           "samples": sum(c.get("samples", 0) for c in items)}
-    return out
+    return {"sm_mhz": statistics.median(sms) if sms else None,
+            "sm_max_mhz": max((c["sm_max_mhz"] for c in items if c.get("sm_max_mhz")), default=None),
+            "reasons": sorted({r for c in items for r in c.get("reasons", [])}),
+            "samples": sum(c.get("samples", 0) for c in items)}
 
 
-def cpu_reference(g: dict, blocks: int, steps: int, warmup: int, min_seconds: float = 0.0) -> dict:
+# ---------------------------------------------------------------------------
+# Verification (outside every timed region)
+# ---------------------------------------------------------------------------
+
+def block_fingerprints(cache: torch.Tensor, chunk: int = 256) -> torch.Tensor:
+    """64-bit fingerprint of every block of a [2, L, N, ...] cache, on the
+    device: per (plane, layer) a wrapping dot product of the block's 64-bit
+    words with fixed random odd weights, folded over planes and layers. Any
+    single changed word changes it (odd weights are invertible mod 2^64)."""
+    L, N = cache.shape[1], cache.shape[2]
+    words = cache[0, 0, 0].numel() * cache.element_size() // 8
+    gen = torch.Generator().manual_seed(97)
+    w = (torch.randint(-2**62, 2**62, (words,), generator=gen, dtype=torch.int64) * 2 + 1).to(cache.device)
+    fp = torch.zeros(N, dtype=torch.int64, device=cache.device)
+    for kv in range(2):
+        for layer in range(L):
+            x = cache[kv, layer].reshape(N, -1).view(torch.int64)
+            h = torch.cat([(x[i:i + chunk] * w).sum(dim=1) for i in range(0, N, chunk)])
+            fp.mul_(FP_MULT).add_(h)
+    return fp
+
+
+def untouched_unchanged(before: torch.Tensor, after: torch.Tensor, written: list[int]) -> dict:
+    keep = torch.ones(before.numel(), dtype=torch.bool, device=before.device)
+    if written:
+        keep[torch.tensor(sorted(set(written)), dtype=torch.long, device=before.device)] = False
+    changed = int(((before != after) & keep).sum().item())
+    return {"blocks_checked": int(keep.sum().item()), "blocks_changed": changed}
+
+
+def verify_local(cache: torch.Tensor, src_ids: list[int], dst_ids: list[int]) -> dict:
+    """1 GPU: every destination chunk equals its source chunk byte for byte."""
+    dev = cache.device
+    s = torch.tensor(src_ids, dtype=torch.long, device=dev)
+    d = torch.tensor(dst_ids, dtype=torch.long, device=dev)
+    bad = torch.zeros((), dtype=torch.int64, device=dev)
+    for kv in range(2):
+        for layer in range(cache.shape[1]):
+            a = cache[kv, layer].index_select(0, s).view(torch.int16).reshape(len(src_ids), -1)
+            b = cache[kv, layer].index_select(0, d).view(torch.int16).reshape(len(dst_ids), -1)
+            bad += (a != b).any(dim=1).sum()
+    return {"chunks_checked": 2 * cache.shape[1] * len(src_ids), "chunks_mismatched": int(bad.item())}
+
+
+def verify_moves(cache: torch.Tensor, outgoing: dict, incoming: dict, dist) -> dict:
+    """N GPUs: compare every moved chunk with what the reference's algorithm
+    delivers on the same GPUs (kv_transfer.py:463-470): per (plane, layer)
+    each source index_selects its blocks and NCCL-sends them, each
+    destination receives them and compares byte for byte with the blocks the
+    kernel wrote. ``outgoing`` = {dst: src ids}, ``incoming`` = {src: dst
+    ids}, positionally matched with the peer's lists. Sums over ranks."""
+    dev = cache.device
+    out_idx = {d: torch.tensor(v, dtype=torch.long, device=dev) for d, v in outgoing.items() if v}
+    in_idx = {s: torch.tensor(v, dtype=torch.long, device=dev) for s, v in incoming.items() if v}
+    bad = torch.zeros((), dtype=torch.int64, device=dev)
+    checked = 0
+    for kv in range(2):
+        for layer in range(cache.shape[1]):
+            plane = cache[kv, layer]
+            sends = {d: plane.index_select(0, idx) for d, idx in out_idx.items()}
+            recvs = {s: torch.empty((len(idx), *plane.shape[1:]), dtype=plane.dtype, device=dev)
+                     for s, idx in in_idx.items()}
+            ops = [dist.P2POp(dist.isend, t, d) for d, t in sends.items()] + \
+                  [dist.P2POp(dist.irecv, t, s) for s, t in recvs.items()]
+            if ops:
+                for work in dist.batch_isend_irecv(ops):
+                    work.wait()
+            for s, idx in in_idx.items():
+                mine = plane.index_select(0, idx).view(torch.int16).reshape(len(idx), -1)
+                bad += (mine != recvs[s].view(torch.int16).reshape(len(idx), -1)).any(dim=1).sum()
+                checked += len(idx)
+    t = torch.tensor([int(bad.item()), checked], dtype=torch.int64, device=dev)
+    dist.all_reduce(t)
+    return {"chunks_checked": int(t[1]), "chunks_mismatched": int(t[0])}
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (the reference's path on the host cores)
+# ---------------------------------------------------------------------------
+
+def cpu_reference_c_port(g: dict, blocks: int, steps: int, warmup: int, min_seconds: float = 0.0) -> dict:
     """The reference algorithm (pack into a payload, then unpack; kv_transfer.py:229-276)
     on the host cores through the C oracle, on a bounded sample of the workload."""
     from oracle import c_oracle
 
     threads = c_oracle.default_threads()
-    torch.set_num_threads(threads)
     n = 2 * blocks + 64
     shape = (2, g["L"], n, g["bs"], g["H"], g["D"])
     cache = torch.zeros(shape, dtype=torch.bfloat16)
@@ -196,12 +307,39 @@ def cpu_reference(g: dict, blocks: int, steps: int, warmup: int, min_seconds: fl
             "ms_per_step": mean * 1e3, "steps": len(times)}
 
 
-# ---------------------------------------------------------------------------
-# 1 GPU: config 2
-# ---------------------------------------------------------------------------
+def cpu_baseline_gloo(g: dict, blocks: int, both_ways: bool, seconds: float) -> dict:
+    """The reference path on CPU tensors with gloo (oracle/torch_ref.py):
+    index_select pack -> gloo send/recv -> index_copy_ unpack between two
+    spawned ranks on this host's cores."""
+    from oracle import torch_ref
 
-STORE = dict(L=80, H=8, D=128, bs=16, N=4096, T=256)
+    r = torch_ref.time_gloo_pair(g, blocks, both_ways=both_ways, min_seconds=seconds)
+    what = "0->1 then 1->0 (two sequential swap_in, as one pair serves both directions)" if both_ways \
+        else "one direction 0->1"
+    return {"value": r["GB/s"], "unit": "GB/s", "cores": r["cores"], "kind": "port",
+            "sample": f"LMPool's swap_in planned path restated with its torch ops (kv_transfer.py:229-276, "
+                      f":463-470) on CPU tensors: 2 spawned gloo ranks (127.0.0.1) x {r['threads_per_rank']} "
+                      f"threads, {blocks} blocks of the same geometry per transfer ({what}), caches of "
+                      f"{r['cache_blocks']} blocks (cost scales with blocks moved, not cache size), "
+                      f"{r['steps']} timed steps ({r['total_s']:.1f} s), verified={r['verified']}",
+            "ms_per_step": r["seconds_per_step"] * 1e3, "steps": r["steps"], "host": r["host"]}
 
+
+def cpu_baseline_local(g: dict, blocks: int, seconds: float) -> dict:
+    from oracle import torch_ref
+
+    r = torch_ref.time_local(g, blocks, min_seconds=seconds)
+    return {"value": r["GB/s"], "unit": "GB/s", "cores": r["cores"], "kind": "port",
+            "sample": f"LMPool's _pack_all_layer_blocks + _unpack_all_layer_blocks restated with its torch ops "
+                      f"(index_select / index_copy_, kv_transfer.py:229-276) in one process on "
+                      f"{r['cores']} threads, {blocks} blocks of the same geometry, cache of {r['cache_blocks']} "
+                      f"blocks, {r['steps']} timed steps ({r['total_s']:.1f} s), verified={r['verified']}",
+            "ms_per_step": r["seconds_per_step"] * 1e3, "steps": r["steps"], "host": r["host"]}
+
+
+# ---------------------------------------------------------------------------
+# 1 GPU: config 2 and store_kvcache
+# ---------------------------------------------------------------------------
 
 def reference_gpu_local(cache: torch.Tensor, L: int, src_ids: list[int], dst_ids: list[int], steps: int) -> dict:
     """The reference's own GPU algorithm on the same device and data, restated
@@ -238,14 +376,30 @@ def reference_gpu_local(cache: torch.Tensor, L: int, src_ids: list[int], dst_ids
             "launches_per_step": 4 * L, "ms_per_step": ms, "GB/s": P / (ms * 1e-3) / 1e9}
 
 
+def reference_store_kvcache_step(keys, values, cache, slots, block_size: int) -> None:
+    """LMPool's store_kvcache (attention.py:24-64, one program per (token,
+    kv head) writing row `slot` of the flat cache unless slot == -1),
+    restated with torch ops per layer as Attention.forward calls it
+    (attention.py:490-507): the valid tokens are selected once per step
+    (slot_mapping is shared by every layer), then per layer the K and V rows
+    are index_copy_'d into the flattened caches. Comparison leg only."""
+    L, T, H, D = keys.shape
+    valid = (slots != -1).nonzero().flatten()
+    rows = slots.index_select(0, valid)
+    for layer in range(L):
+        cache[0, layer].view(-1, H, D).index_copy_(0, rows, keys[layer].index_select(0, valid))
+        cache[1, layer].view(-1, H, D).index_copy_(0, rows, values[layer].index_select(0, valid))
+
+
 def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: int = 0) -> dict:
     """store_kvcache at benchmark config 5 geometry (L=80, H=8, D=128,
     block_size=16, T=256 tokens per step, ~10% padding slots; the cache is
     shrunk to 4096 blocks: the cost does not depend on N). A step writes every
     layer: 80 single-layer launches as the model issues them (eager, and
     captured in a CUDA graph as the decode path does), or one all-layer
-    launch. L2 is flushed (written, then another buffer read) between timed
-    steps."""
+    launch; beside them the reference's algorithm restated with torch ops.
+    L2 is flushed (written, then another buffer read) between timed steps.
+    Every leg's result is checked against the reference leg's."""
     from lmpool_b200.attention import store_kvcache, store_kvcache_layers
     from lmpool_b200.kv_transfer import check_device_status
 
@@ -272,8 +426,19 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: 
     def all_layers():
         store_kvcache_layers(keys, values, cache, slots, c["bs"])
 
-    per_layer()
-    all_layers()
+    def reference():
+        reference_store_kvcache_step(keys, values, cache, slots, c["bs"])
+
+    # correctness of every leg against the reference leg, on the same start
+    start = cache.clone()
+    reference()
+    expect = cache.clone()
+    results = {}
+    for name, fn in (("per_layer", per_layer), ("all_layers", all_layers)):
+        cache.copy_(start)
+        fn()
+        results[name] = bool(torch.equal(cache.view(torch.int16), expect.view(torch.int16)))
+    del start, expect
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
@@ -297,6 +462,7 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: 
     ms_eager = timed(per_layer)
     ms_graph = timed(graph.replay)
     ms_all = timed(all_layers)
+    ms_ref = timed(reference)
     check_device_status(dev_idx)
     row = c["H"] * c["D"] * 2
     traffic = c["L"] * (2 * c["T"] * row + 2 * valid * row + c["T"] * 8)
@@ -305,11 +471,17 @@ def bench_store_kvcache(dev_idx: int, peak: float, iters: int = 30, num_blocks: 
 
     def entry(ms, launches):
         gbs = traffic / (ms * 1e-3) / 1e9
-        return {"ms_per_step": ms, "launches_per_step": launches, "GB/s": gbs, "frac_hbm": gbs / peak}
+        return {"ms_per_step": ms, "us_per_layer": ms * 1e3 / c["L"], "launches_per_step": launches, "GB/s": gbs,
+                "frac_hbm": gbs / peak}
 
     return {"geometry": dict(c, valid_tokens=valid), "bytes_per_step": traffic,
             "per_layer_eager": entry(ms_eager, c["L"]), "per_layer_graph": entry(ms_graph, c["L"]),
             "all_layers_one_launch": entry(ms_all, 1),
+            "reference_torch_ops": dict(entry(ms_ref, None), algorithm=(
+                "attention.py:24-64 restated with torch ops per layer (valid slots selected once per step, "
+                "then index_copy_ of K and V rows per layer), eager")),
+            "speedup_per_layer_graph_vs_reference": ms_ref / ms_graph,
+            "bit_exact_vs_reference": results,
             "note": "bytes = per layer: read K,V rows of all T tokens + write K,V rows of valid tokens + slot ids"}
 
 
@@ -341,6 +513,7 @@ def bench_local(args) -> dict:
     B = g["B"]
     src_t, dst_t = ids_for(B)
     P = payload_bytes(g, B)
+    fp_before = None if args.quick else block_fingerprints(cache)
 
     def step():
         kt._launch_move(dev_idx, lay, lay, src_t, dst_t, B, status, stream)
@@ -360,21 +533,19 @@ def bench_local(args) -> dict:
     ms = start.elapsed_time(end) / args.steps
     if int(status.item()) != 0:
         raise RuntimeError(f"kernel status {status.item()}")
-    # correctness spot check of the timed workload
-    for i in (0, B // 2, B - 1):
-        if not torch.equal(cache[:, :, perm[B + i]].view(torch.int16), cache[:, :, perm[i]].view(torch.int16)):
-            raise RuntimeError("moved block differs from its source")
-
     value = P / (ms * 1e-3) / 1e9
     peak, peak_src = hbm_peak()
     achieved = 2 * P / (ms * 1e-3) / 1e9
-    traffic = profile_traffic("move_local_config2")
+    traffic = profile_value("move_local_config2", "dram_bytes_per_launch_full_size")
     if args.quick:
         print(json.dumps({"quick": True, "blocks": B, "cache_blocks": g["N"], "ms_per_step": ms, "GB/s": value,
                           "hbm_GB/s": achieved, "frac": achieved / peak}), flush=True)
         return None
+    verification = {"moved": verify_local(cache, perm[:B], perm[B:2 * B]),
+                    "untouched": untouched_unchanged(fp_before, block_fingerprints(cache), perm[B:2 * B])}
 
-    # B sweep, L2 flushed before each timed launch (clean, and write-only)
+    # B sweep, L2 flushed before each timed launch (clean, and write-only);
+    # every swept move checked byte for byte after its timing
     flush = L2Flush(dev)
     sweep = []
     for b in SWEEP_B:
@@ -396,10 +567,14 @@ def bench_local(args) -> dict:
                 times.append(e0.elapsed_time(e1))
             med[dirty] = statistics.median(times) * 1e-3
         t = med[False]
+        chk = verify_local(cache, perm[:b], perm[b:2 * b])
         sweep.append({"blocks": b, "bytes": pb, "ms": t * 1e3, "GB/s": pb / t / 1e9,
                       "hbm_GB/s": 2 * pb / t / 1e9, "frac_hbm": 2 * pb / t / 1e9 / peak,
-                      "ms_dirty_l2": med[True] * 1e3, "frac_hbm_dirty_l2": 2 * pb / med[True] / 1e9 / peak})
+                      "ms_dirty_l2": med[True] * 1e3, "frac_hbm_dirty_l2": 2 * pb / med[True] / 1e9 / peak,
+                      "verified_bitexact": chk["chunks_mismatched"] == 0})
     del flush
+    if int(status.item()) != 0:
+        raise RuntimeError(f"kernel status {status.item()}")
 
     # end to end through the public API: host id lists -> pinned -> device,
     # one launch, device -> host status read, every step
@@ -423,26 +598,33 @@ def bench_local(args) -> dict:
     del cache
     torch.cuda.empty_cache()
     store = bench_store_kvcache(dev_idx, peak)
-    cpu = cpu_reference(g, CPU_SAMPLE_BLOCKS, steps=3, warmup=1, min_seconds=10.0)
+    cpu = cpu_baseline_gloo(g, CPU_SAMPLE_BLOCKS, both_ways=False, seconds=10.0)
+    cpu_local = cpu_baseline_local(g, CPU_SAMPLE_BLOCKS, seconds=8.0)
+    cpu_c = cpu_reference_c_port(g, CPU_SAMPLE_BLOCKS, steps=3, warmup=1, min_seconds=8.0)
+    ok = verification["moved"]["chunks_mismatched"] == 0 and verification["untouched"]["blocks_changed"] == 0 \
+        and all(r["verified_bitexact"] for r in sweep) and all(store["bit_exact_vs_reference"].values())
     return {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: bf16 N(0,1) KV cache (device generator seed 0), block ids from randperm(2048, seed 0)",
-        "config": {"workload": g["workload"], "num_layers": g["L"], "num_blocks": g["N"], "block_size": g["bs"],
-                   "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_moved": B, "payload_bytes_per_step": P,
-                   "src_ids": "randperm[:512]", "dst_ids": "randperm[512:1024]",
-                   "l2": "inputs larger than L2 (15 GB read + 15 GB written per step); the sweep flushes L2 "
-                         "before each launch by writing 512 MB then reading 512 MB (ms_dirty_l2: write only)",
-                   "parallelism": "replicas only"},
+        "config": line_config(g, 1),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_src,
                      "algorithmic_bytes_per_launch": 2 * P, "kernel_ms": ms},
         "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline_host": cpu["host"],
+        "cpu_baseline_local": {k: cpu_local[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline_c_port": {k: cpu_c[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": P / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 4,
                 "api": "lmpool_b200.kv_transfer.move_blocks(host id lists, synchronize=True)"},
         "gpu_launches": args.steps,
         "clocks": clk,
+        "verified_bitexact": ok,
+        "verification": dict(verification, method=(
+            "moved: every (plane, layer, block) chunk of the timed workload compared byte for byte with its "
+            "source on the device; untouched: 64-bit per-block fingerprints before and after; sweep: each "
+            "swept move compared byte for byte after its timing")),
         "sweep": sweep,
         "reference_gpu_path": ref_gpu,
         "store_kvcache": store,
@@ -451,30 +633,59 @@ def bench_local(args) -> dict:
 
 
 # ---------------------------------------------------------------------------
-# N GPUs: config 4 phase A
+# N GPUs: configs 3, 4 and 5
 # ---------------------------------------------------------------------------
 
-def block_sums(cache: torch.Tensor, ids: list[int]) -> torch.Tensor:
-    """Per (plane, layer, block) sum of the bf16 bit patterns of the listed
-    blocks, int64, one (plane, layer) slice at a time (bounded temporaries)."""
-    idx = torch.tensor(ids, dtype=torch.int64, device=cache.device)
-    out = torch.empty(2, cache.shape[1], len(ids), dtype=torch.int64, device=cache.device)
-    for kv in range(2):
-        for layer in range(cache.shape[1]):
-            sel = cache[kv, layer].index_select(0, idx).view(torch.int16).reshape(len(ids), -1)
-            out[kv, layer] = sel.sum(-1, dtype=torch.int64)
-    return out.cpu()
+def all_partner_sets(N: int, world: int, r: int, B: int = PHASE_B_BLOCKS):
+    """(incoming targets by source, outgoing sources by destination) of rank r
+    in benchmark config 4 phase B: seeded-random blocks, the incoming sets
+    disjoint from each other and from every outgoing set."""
+    others = [x for x in range(world) if x != r]
+    perm = seeded_perm(N, 5000 + r)
+    inc = {s: perm[i * B:(i + 1) * B] for i, s in enumerate(others)}
+    pool = perm[B * len(others):]
+    out = {}
+    for d in others:
+        sel = seeded_perm(len(pool), 6000 + 16 * r + d)[:B]
+        out[d] = [pool[i] for i in sel]
+    return inc, out
 
 
-def pair_sweep(ep, link, g: dict, rank: int, stream, dist, mode: str) -> list[dict]:
+def timed_max(dist, dev, stream, fn, reps: int) -> float:
+    """ms per call of ``fn`` over ``reps`` back-to-back calls, CUDA events on
+    ``stream``, between a barrier and a synchronize; max over ranks."""
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def scrub(cache: torch.Tensor, ids: list[int]) -> None:
+    """Zero the listed blocks, so that a verification after the next move
+    shows that move's bytes and not an earlier one's."""
+    if ids:
+        cache[:, :, torch.tensor(sorted(set(ids)), dtype=torch.long, device=cache.device)] = 0
+
+
+def pair_sweep(ep, cache, g: dict, rank: int, stream, dist, mode: str) -> list[dict]:
     """benchmark config 3 on ranks 0 -> 1: B in {1, 8, 64, 256}, contiguous and
     scattered source ids. Each timed run is K back-to-back transfers in the
-    configured mode, cycling through disjoint id sets so no transfer re-reads
-    blocks still in L2; time = max over the two ranks."""
+    given mode, cycling through disjoint id sets so no transfer re-reads
+    blocks still in L2; time = max over the two ranks. The destination
+    blocks are zeroed before each case, which is then verified byte for byte
+    against the reference's algorithm."""
     dev = torch.device("cuda", ep.device)
     N = g["N"]
     out = []
-    for B in (1, 8, 64, 256):
+    for B in PAIR_SWEEP_B:
         for ids_kind in ("contiguous", "scattered"):
             K = 20 if B <= 64 else 8
             nsets = max(1, min(K, (N // 2) // B))
@@ -489,35 +700,32 @@ def pair_sweep(ep, link, g: dict, rank: int, stream, dist, mode: str) -> list[di
             dst_sets = [dperm[i * B:(i + 1) * B] for i in range(nsets)]
             src_t = [torch.tensor(x, dtype=torch.int64, device=dev) for x in src_sets]
             dst_t = [torch.tensor(x, dtype=torch.int64, device=dev) for x in dst_sets]
+            k_box = [0]
 
-            def one(k):
+            def one():
+                k = k_box[0] % nsets
+                k_box[0] += 1
                 if rank == 1:
-                    ep.exchange(mode, ep.cache, [], [(0, src_t[k % nsets], dst_t[k % nsets], B)], 60.0, stream)
+                    ep.exchange(mode, ep.cache, [], [(0, src_t[k], dst_t[k], B)], 60.0, stream)
                 else:
-                    ep.exchange(mode, ep.cache, [(1, src_t[k % nsets], B)], [], 60.0, stream)
+                    ep.exchange(mode, ep.cache, [(1, src_t[k], B)], [], 60.0, stream)
 
-            for k in range(3):
-                one(k)
-            torch.cuda.synchronize()
-            dist.barrier()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for k in range(K):
-                one(k)
-            e1.record(stream)
-            torch.cuda.synchronize()
-            t = torch.tensor([e0.elapsed_time(e1) / K], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+            flat_src = [b for s in src_sets for b in s]
+            flat_dst = [b for s in dst_sets for b in s]
+            if rank == 1:
+                scrub(cache, flat_dst)
+            for _ in range(3):
+                one()
+            ms = timed_max(dist, dev, stream, one, K)
+            chk = verify_moves(cache, {1: flat_src} if rank == 0 else {}, {0: flat_dst} if rank == 1 else {}, dist)
             pb = payload_bytes(g, B)
             out.append({"mode": mode, "blocks": B, "ids": ids_kind, "bytes": pb, "ms": ms,
-                        "GB/s": pb / (ms * 1e-3) / 1e9,
-                        "frac_nvlink": pb / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS})
+                        "GB/s": pb / (ms * 1e-3) / 1e9, "frac_nvlink": pb / (ms * 1e-3) / 1e9 / NVLINK_NOMINAL_GBS,
+                        "verified_bitexact": chk["chunks_mismatched"] == 0, "chunks_checked": chk["chunks_checked"]})
     return out
 
 
-def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, blocks=(1, 8, 64, 256)) -> dict:
+def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, blocks=PAIR_SWEEP_B) -> dict:
     """The reference's planned swap_in on the same two GPUs, restated with the
     same ops (kv_transfer.py:463-470): rank 0 packs with 2*L index_select and
     NCCL-sends the payload, rank 1 receives it and unpacks with 2*L
@@ -558,18 +766,10 @@ def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, blocks=(1,
             torch.cuda.synchronize()
             if k >= 3:
                 times.append((time.perf_counter() - t0) * 1e3)
-        # the same transfers back to back, timed on the device like pair_sweep
-        dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(iters):
-            one()
-        e1.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([statistics.mean(times), e0.elapsed_time(e1) / iters], dtype=torch.float64, device=dev)
+        ms_dev = timed_max(dist, dev, torch.cuda.current_stream(dev), one, iters)
+        t = torch.tensor([statistics.mean(times)], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_wall, ms_dev = float(t[0].item()), float(t[1].item())
+        ms_wall = float(t.item())
         P = payload_bytes(g, B)
         out.append({"blocks": B, "ms": ms_dev, "GB/s": P / (ms_dev * 1e-3) / 1e9,
                     "ms_wall": ms_wall, "GB/s_wall": P / (ms_wall * 1e-3) / 1e9})
@@ -582,6 +782,53 @@ def reference_gpu_pair(cache: torch.Tensor, g: dict, rank: int, dist, blocks=(1,
                       "the two by this kernel's best device-timed scattered transfer",
             "blocks": head["blocks"], "ms": head["ms"], "GB/s": head["GB/s"], "ms_wall": head["ms_wall"],
             "sweep": out}
+
+
+def reference_phase_a(cache: torch.Tensor, g: dict, rank: int, world: int, dist, src_ids, partner_src, dst_ids,
+                      iters: int = 5) -> dict:
+    """Phase A with the reference's algorithm on the same GPUs: per pair, the
+    two directions as two sequential planned swap_in calls (LMPool runs one
+    plan per pair at a time; two opposite NCCL swaps at once would block each
+    other on the pair's stream): pack (2*L index_select) -> NCCL send/recv ->
+    unpack (2*L index_copy_), 0->1 then 1->0. Device-timed, max over ranks."""
+    dev = cache.device
+    L, B = g["L"], g["B"]
+    partner = rank + 1 if rank % 2 == 0 else rank - 1
+    out_idx = torch.tensor(src_ids, dtype=torch.long, device=dev)
+    in_idx = torch.tensor(dst_ids, dtype=torch.long, device=dev)
+    shape = (L, 2, B, *cache.shape[3:])
+
+    def send():
+        payload = torch.empty(shape, dtype=cache.dtype, device=dev)
+        for layer in range(L):
+            torch.index_select(cache[0, layer], 0, out_idx, out=payload[layer, 0])
+            torch.index_select(cache[1, layer], 0, out_idx, out=payload[layer, 1])
+        dist.send(payload, dst=partner)
+
+    def recv():
+        payload = torch.empty(shape, dtype=cache.dtype, device=dev)
+        dist.recv(payload, src=partner)
+        for layer in range(L):
+            cache[0, layer].index_copy_(0, in_idx, payload[layer, 0])
+            cache[1, layer].index_copy_(0, in_idx, payload[layer, 1])
+
+    def one():
+        if rank % 2 == 0:
+            send()
+            recv()
+        else:
+            recv()
+            send()
+
+    for _ in range(2):
+        one()
+    ms = timed_max(dist, dev, torch.cuda.current_stream(dev), one, iters)
+    torch.cuda.empty_cache()
+    P = payload_bytes(g, B)
+    return {"algorithm": "per pair: two sequential planned swap_in (index_select -> NCCL send/recv -> index_copy_, "
+                         "kv_transfer.py:463-470), 0->1 then 1->0", "ms_per_step": ms,
+            "value": world * P / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "GB/s_per_direction_averaged": P / (ms * 1e-3) / 1e9}
 
 
 def reference_all_partner(cache: torch.Tensor, g: dict, rank: int, world: int, dist, iters: int = 5) -> dict:
@@ -614,8 +861,8 @@ def reference_all_partner(cache: torch.Tensor, g: dict, rank: int, world: int, d
                 cache[0, layer].index_copy_(0, in_idx[s], recv[s][layer, 0])
                 cache[1, layer].index_copy_(0, in_idx[s], recv[s][layer, 1])
 
-    # the kernel legs just wrote these blocks from the same sources
-    before = {s: block_sums(cache, v) for s, v in incoming.items()}
+    written = [b for v in incoming.values() for b in v]
+    fp_before = block_fingerprints(cache)     # the kernel legs just wrote these blocks from the same sources
     times = []
     for k in range(2 + iters):
         dist.barrier()
@@ -628,7 +875,8 @@ def reference_all_partner(cache: torch.Tensor, g: dict, rank: int, world: int, d
     t = torch.tensor([statistics.mean(times)], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    same = all(torch.equal(before[s], block_sums(cache, v)) for s, v in incoming.items())
+    fp_after = block_fingerprints(cache)
+    same = bool(torch.equal(fp_before, fp_after))
     agree = [None] * world
     dist.all_gather_object(agree, same)
     del send, recv
@@ -638,7 +886,8 @@ def reference_all_partner(cache: torch.Tensor, g: dict, rank: int, world: int, d
     return {"algorithm": "index_select pack -> NCCL batched send/recv -> index_copy_ unpack",
             "blocks_per_destination": B, "ms_per_step": ms,
             "value": world * (world - 1) * pb / (ms * 1e-3) / 1e9, "unit": "GB/s",
-            "per_gpu_egress_GB/s": per_gpu_out, "same_blocks_as_kernel": all(agree)}
+            "per_gpu_egress_GB/s": per_gpu_out, "blocks_rewritten": len(written),
+            "same_blocks_as_kernel": all(agree)}
 
 
 def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: str,
@@ -672,36 +921,229 @@ def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: s
         raise ValueError(f"unknown schedule {schedule!r}")
 
     ep.status.zero_()
+    written = [b for v in incoming.values() for b in v]
+    scrub(cache, written)
+    fp_before = block_fingerprints(cache)
     for _ in range(3):
         step()
-    K = 10
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(K):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / K], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    mine = {"rank": rank, "bits": int(ep.status.item()),
-            "out": {d: block_sums(cache, v) for d, v in outgoing.items()},
-            "in": {s: block_sums(cache, v) for s, v in incoming.items()}}
-    gathered: list = [None] * world
-    dist.all_gather_object(gathered, mine)
-    ok = all(x["bits"] == 0 for x in gathered)
-    for x in gathered:
-        for d, sums in x["out"].items():
-            ok &= torch.equal(sums, gathered[d]["in"][x["rank"]])
+    ms = timed_max(dist, dev, stream, step, 10)
+    bits = int(ep.status.item())
+    chk = verify_moves(cache, outgoing, incoming, dist)
+    unt = untouched_unchanged(fp_before, block_fingerprints(cache), written)
+    oks: list = [None] * world
+    dist.all_gather_object(oks, bits == 0 and unt["blocks_changed"] == 0)
+    ok = all(oks) and chk["chunks_mismatched"] == 0
     pb = payload_bytes(g, B)
     per_gpu_out = (world - 1) * pb / (ms * 1e-3) / 1e9
-    return {"ok": bool(ok), "schedule": schedule, "blocks_per_destination": B, "ms_per_step": ms,
+    return {"ok": bool(ok), "schedule": schedule, "mode": mode, "blocks_per_destination": B, "ms_per_step": ms,
             "value": world * (world - 1) * pb / (ms * 1e-3) / 1e9, "unit": "GB/s",
-            "per_gpu_egress_GB/s": per_gpu_out, "frac_nvlink_per_gpu_egress": per_gpu_out / NVLINK_PEER_GBS,
-            "verified": bool(ok)}
+            "per_gpu_egress_GB/s": per_gpu_out, "frac_nvlink_per_gpu_egress": per_gpu_out / NVLINK_NOMINAL_GBS,
+            "verified_bitexact": bool(ok), "chunks_checked": chk["chunks_checked"]}
+
+
+def peer_copy(ep, partner: int, rank: int, stream, dist, nbytes: int = 2 << 30) -> dict | None:
+    """Plain peer copies over the same NVLink, for the record beside the
+    kernel: cudaMemcpyAsync (copy engine) from the partner's cache (through
+    this process's IPC mapping) into a local buffer, timed with CUDA events,
+    one direction (even ranks copy, odd ranks idle) and both at once. Only
+    reads the partner's memory."""
+    try:
+        from cuda.bindings import runtime as rt
+    except ImportError:
+        return None
+    dev = torch.device("cuda", ep.device)
+    link = ep.get_link(partner)
+    src_ptr = link.cache.base
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+    def cp(active: bool):
+        if active:
+            err, = rt.cudaMemcpyAsync(dst.data_ptr(), src_ptr, nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                      stream.cuda_stream)
+            if err != rt.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"cudaMemcpyAsync: {err}")
+
+    for _ in range(2):
+        cp(True)
+    one = timed_max(dist, dev, stream, lambda: cp(rank % 2 == 0), 5)
+    both = timed_max(dist, dev, stream, lambda: cp(True), 5)
+    del dst
+    torch.cuda.empty_cache()
+    return {"method": "cudaMemcpyAsync from the partner's memory (IPC mapping) into local HBM, 2 GiB, CUDA events, "
+                      "max over ranks",
+            "one_direction_GB/s": nbytes / (one * 1e-3) / 1e9, "both_directions_GB/s_per_direction":
+                nbytes / (both * 1e-3) / 1e9}
+
+
+def e2e_swap_in(kt, cache, g, rank: int, partner: int, src_ids, partner_src, dst_ids, stream, dist,
+                steps: int) -> dict:
+    """Phase A end to end through the reference-facing API: per pair, swap_in
+    0->1 then swap_in 1->0 (LMPool's data plane issues one plan per pair at a
+    time, ModelRunner.execute_swap_out/in -> swap_in(negotiate_blocks=False),
+    model_runner.py:747-806), host id lists in, status read back, in the
+    process's transfer mode (pull). Also the source's call latency with the
+    source returning after the read and once its grant is enqueued."""
+    L, bs, H, D = g["L"], g["bs"], g["H"], g["D"]
+    dev = torch.device("cuda", kt._local_device(rank))
+    even = rank % 2 == 0
+
+    def as_source():
+        kt.swap_in(rank, src_ids, partner, cache, L, bs, H, D, negotiate_blocks=False)
+
+    def as_destination():
+        kt.swap_in(partner, partner_src, rank, cache, L, bs, H, D, local_target_blocks=dst_ids,
+                   negotiate_blocks=False)
+
+    def step():
+        if even:
+            as_source()
+            as_destination()
+        else:
+            as_destination()
+            as_source()
+
+    for _ in range(2):
+        step()
+    ms = timed_max(dist, dev, stream, step, steps)
+    # the source's call latency (host wall clock), both settings of LMPOOL_B200_SOURCE_RETURN
+    lat = {}
+    old = os.environ.get("LMPOOL_B200_SOURCE_RETURN")
+    for setting in ("read", "granted"):
+        os.environ["LMPOOL_B200_SOURCE_RETURN"] = setting
+        vals = []
+        for _ in range(5):
+            torch.cuda.synchronize()
+            dist.barrier()
+            if even:
+                t0 = time.perf_counter()
+                as_source()
+                vals.append((time.perf_counter() - t0) * 1e3)
+            else:
+                as_destination()
+            torch.cuda.synchronize()
+        if even:
+            lat[setting] = statistics.median(vals)
+    if old is None:
+        os.environ.pop("LMPOOL_B200_SOURCE_RETURN", None)
+    else:
+        os.environ["LMPOOL_B200_SOURCE_RETURN"] = old
+    kt._ENDPOINTS[dev.index].poll_deferred(wait=True)
+    return {"ms_per_step": ms, "source_call_ms": lat}
+
+
+def config5_leg(kt, rank: int, world: int, dist, steps: int, mode: str) -> dict:
+    """benchmark config 5 on the pairs: the transfer alone, store_kvcache
+    alone, and both at once on two streams. The cache is shrunk from 65536 to
+    16384 blocks per rank (80 GiB; 65536 would be 320 GiB): transfer and store
+    costs depend on B and T, not on N. Transfers verified byte for byte
+    against the reference's algorithm; every stored row checked."""
+    from lmpool_b200.attention import store_kvcache, store_kvcache_layers
+
+    c = CONFIG5
+    local = kt._local_device(rank)
+    dev = torch.device("cuda", local)
+    cache = torch.empty((2, c["L"], c["N"], c["bs"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    cache.normal_(generator=gen)
+    keys = torch.empty((c["L"], c["T"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev).normal_(generator=gen)
+    values = torch.empty_like(keys).normal_(generator=gen)
+    kt.register_kv_cache(cache, c["L"])
+    pairs = [(r, r + 1) for r in range(0, world, 2)]
+    kt.prewarm_p2p_pairs(pairs, num_layers=c["L"], block_size=c["bs"], num_kv_heads=c["H"], head_dim=c["D"],
+                         num_blocks=2, dtype=torch.bfloat16, timeout_s=60)
+    partner = rank + 1 if rank % 2 == 0 else rank - 1
+    B = c["B"]
+    perm = seeded_perm(c["N"], 7000 + rank)
+    src_ids, dst_ids = perm[:B], perm[B:2 * B]          # fragmented, disjoint
+    partner_src = seeded_perm(c["N"], 7000 + partner)[:B]
+    # store_kvcache slots avoid both transfer sets (blocks being moved are
+    # locked: the model never writes them)
+    busy = torch.zeros(c["N"], dtype=torch.bool)
+    busy[src_ids] = True
+    busy[dst_ids] = True
+    free_blocks = (~busy).nonzero().flatten()
+    g = torch.Generator().manual_seed(77 + rank)
+    pick = free_blocks[torch.randperm(len(free_blocks), generator=g)[:c["T"]]]
+    slots = pick * c["bs"] + torch.randint(0, c["bs"], (c["T"],), generator=g)
+    slots[torch.rand(c["T"], generator=g) < 0.1] = -1
+    slots = slots.to(torch.int64).to(dev)
+    ep = kt._ENDPOINTS[local]
+    xs = torch.cuda.Stream(dev)
+    ss = torch.cuda.Stream(dev)
+    src_t = torch.tensor(src_ids, dtype=torch.int64, device=dev)
+    dst_t = torch.tensor(dst_ids, dtype=torch.int64, device=dev)
+    psrc_t = torch.tensor(partner_src, dtype=torch.int64, device=dev)
+    P = B * c["L"] * 2 * c["bs"] * c["H"] * c["D"] * 2
+    row = c["H"] * c["D"] * 2
+    valid = int((slots >= 0).sum())
+    store_bytes = c["L"] * (2 * c["T"] * row + 2 * valid * row + c["T"] * 8)
+
+    def xfer():
+        ep.exchange(mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, xs)
+
+    def store_step():
+        with torch.cuda.stream(ss):
+            store_kvcache_layers(keys, values, cache, slots, c["bs"])
+
+    with torch.cuda.stream(ss):
+        for layer in range(c["L"]):   # warm the single-layer launch too
+            store_kvcache(keys[layer], values[layer], cache[0, layer], cache[1, layer], slots, c["bs"])
+    ep.status.zero_()
+    for _ in range(3):
+        xfer()
+        store_step()
+    torch.cuda.synchronize()
+    K = max(3, min(steps, 10))
+    x_ms = timed_max(dist, dev, xs, xfer, K)
+    s_ms = timed_max(dist, dev, ss, store_step, 200)
+    M = max(1, int(K * x_ms / s_ms))
+    # both at once: K transfers on one stream, M store steps on another, same start
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    start.record(torch.cuda.current_stream(dev))
+    xs.wait_event(start)
+    ss.wait_event(start)
+    xe, se = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for k in range(max(K, M)):
+        if k < K:
+            xfer()
+        if k < M:
+            store_step()
+    xe.record(xs)
+    se.record(ss)
+    torch.cuda.synchronize()
+    t = torch.tensor([start.elapsed_time(xe) / K, start.elapsed_time(se) / M], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    xo_ms, so_ms = float(t[0]), float(t[1])
+    bits = int(ep.status.item())
+    kt.check_device_status(local)
+    chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist)
+    vidx = (slots >= 0).nonzero().flatten()
+    vs = slots.index_select(0, vidx)
+    k_rows = cache[0].reshape(c["L"], -1, c["H"], c["D"]).index_select(1, vs)
+    v_rows = cache[1].reshape(c["L"], -1, c["H"], c["D"]).index_select(1, vs)
+    stored_ok = bool(torch.equal(k_rows.view(torch.int16), keys.index_select(1, vidx).view(torch.int16))) and \
+        bool(torch.equal(v_rows.view(torch.int16), values.index_select(1, vidx).view(torch.int16)))
+    oks: list = [None] * world
+    dist.all_gather_object(oks, bits == 0 and stored_ok)
+    kt.shutdown()
+    del cache, keys, values
+    torch.cuda.empty_cache()
+    return {
+        "workload": c["workload"], "config": {k: c[k] for k in ("L", "N", "bs", "H", "D", "B", "T")},
+        "substitution": "num_blocks 65536 -> 16384 per rank (320 GiB does not fit one B200)",
+        "transfer_mode": mode,
+        "transfer_alone": {"ms": x_ms, "GB/s_per_direction": P / (x_ms * 1e-3) / 1e9,
+                           "frac_nvlink": P / (x_ms * 1e-3) / 1e9 / NVLINK_NOMINAL_GBS},
+        "store_alone": {"ms_per_step": s_ms, "GB/s": store_bytes / (s_ms * 1e-3) / 1e9,
+                        "launch": "all 80 layers in one launch"},
+        "overlapped": {"transfers": K, "store_steps": M, "transfer_ms": xo_ms,
+                       "transfer_GB/s_per_direction": P / (xo_ms * 1e-3) / 1e9,
+                       "store_ms_per_step": so_ms, "store_GB/s": store_bytes / (so_ms * 1e-3) / 1e9},
+        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes,
+        "verified_bitexact": all(oks) and chk["chunks_mismatched"] == 0, "chunks_checked": chk["chunks_checked"],
+    }
 
 
 def bench_pairs(args) -> dict | None:
@@ -736,7 +1178,6 @@ def bench_pairs(args) -> dict | None:
     free = [b for b in seeded_perm(g["N"], 2000 + rank) if b not in set(src_ids)]
     dst_ids = free[:B]
     ep = kt._ENDPOINTS[local]
-    link = ep.get_link(partner)
     # Both directions of a pair at once: push measured faster (pull's read
     # requests share each direction with the other flow's data).
     mode = "push" if args.pair_mode == "auto" else args.pair_mode
@@ -750,6 +1191,7 @@ def bench_pairs(args) -> dict | None:
     def step(m=None):
         ep.exchange(m or mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, stream)
 
+    fp_before = block_fingerprints(cache)
     ep.status.zero_()
     for _ in range(args.warmup):
         step()
@@ -770,33 +1212,25 @@ def bench_pairs(args) -> dict | None:
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     bits = int(ep.status.item())
-    # correctness: checksums of what this rank sent vs what its partner holds
-    sums_src = block_sums(cache, src_ids)
-    sums_dst = block_sums(cache, dst_ids)
+    # bit-exact verification of the timed workload (outside the timed region)
+    phase_a_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist)
+    phase_a_unt = untouched_unchanged(fp_before, block_fingerprints(cache), dst_ids)
     gathered: list = [None] * world
-    dist.all_gather_object(gathered, {"rank": rank, "src": sums_src, "dst": sums_dst, "bits": bits, "clk": clk})
-    ok = all(item["bits"] == 0 for item in gathered)
-    ok &= torch.equal(gathered[partner]["src"], sums_dst)
+    dist.all_gather_object(gathered, {"rank": rank, "bits": bits, "clk": clk, "untouched": phase_a_unt})
+    ok = all(item["bits"] == 0 and item["untouched"]["blocks_changed"] == 0 for item in gathered)
+    ok &= phase_a_chk["chunks_mismatched"] == 0
 
     # the same exchange in the other mode, for the record
     for _ in range(3):
         step(other)
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(10):
-        step(other)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    t = torch.tensor([e0.elapsed_time(e1) / 10], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    other_ms = float(t.item())
+    other_ms = timed_max(dist, dev, stream, lambda: step(other), 10)
 
+    copies = peer_copy(ep, partner, rank, stream, dist)
     sweep = None
     if world == 2:   # one direction at a time: both modes, pull is the default of swap_in
-        sweep = pair_sweep(ep, link, g, rank, stream, dist, "pull") + pair_sweep(ep, link, g, rank, stream, dist,
-                                                                               "push")
+        sweep = pair_sweep(ep, cache, g, rank, stream, dist, "pull") + \
+            pair_sweep(ep, cache, g, rank, stream, dist, "push")
+        ok &= all(r["verified_bitexact"] for r in sweep)
     ref_pair = reference_gpu_pair(cache, g, rank, dist) if world == 2 else None
     if ref_pair is not None and sweep is not None:
         for row in [ref_pair] + ref_pair["sweep"]:
@@ -813,65 +1247,100 @@ def bench_pairs(args) -> dict | None:
         ok &= all(v["ok"] for v in phase_b.values())
         phase_b["reference_nccl"] = reference_all_partner(cache, g, rank, world, dist)
 
-    # end to end: host id lists through swap_batch (pinned H2D + status D2H per step)
-    e2e_steps = max(3, min(args.steps, 30))
+    # the reference's algorithm on the same GPUs for the headline workload
+    ref_a = reference_phase_a(cache, g, rank, world, dist, src_ids, partner_src, dst_ids)
+    ref_a["this_kernel_speedup"] = ref_a["ms_per_step"] / ms
+
+    # end to end through swap_in (the API LMPool calls), then through swap_batch;
+    # the destination blocks are zeroed before each and verified after it
+    e2e_steps = max(3, min(args.steps, 20))
+    scrub(cache, dst_ids)
+    e2e_in = e2e_swap_in(kt, cache, g, rank, partner, src_ids, partner_src, dst_ids, stream, dist, e2e_steps)
+    e2e_in_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist)
+    ok &= e2e_in_chk["chunks_mismatched"] == 0
+    scrub(cache, dst_ids)
     for _ in range(2):
         kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode)
-    dist.barrier()
-    torch.cuda.synchronize()
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(e2e_steps):
-        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    t2 = torch.tensor([e2.elapsed_time(e3) / e2e_steps], dtype=torch.float64, device=dev)
-    dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t2.item())
+    batch_ms = timed_max(dist, dev, stream,
+                         lambda: kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode),
+                         e2e_steps)
+    e2e_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist)
+    ok &= e2e_chk["chunks_mismatched"] == 0
+    kt.shutdown()
+    kt._REGISTERED.pop(local, None)
+    del cache
+    ep = None
+    torch.cuda.empty_cache()
+
+    c5 = config5_leg(kt, rank, world, dist, args.steps, mode)
+    ok &= c5["verified_bitexact"]
     oks = [None] * world
     dist.all_gather_object(oks, bool(ok))
-    kt.shutdown()
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
         return None
     if not all(oks):
         raise RuntimeError("pair transfer verification failed")
+    cpu = cpu_baseline_gloo(g, CPU_SAMPLE_BLOCKS, both_ways=True, seconds=10.0)
     value = world * P / (ms * 1e-3) / 1e9
     per_dir = P / (ms * 1e-3) / 1e9
+    wire_per_block = profile_value("push_nvlink_pair", "nvlink_tx_bytes_per_block")
+    traffic = wire_per_block * B if wire_per_block else None
     return {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic: bf16 N(0,1) KV caches (device generator seed = rank), seeded randperm ids",
-        "config": {"workload": g["workload"], "num_layers": g["L"], "num_blocks": g["N"], "block_size": g["bs"],
-                   "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_moved_per_direction": B,
-                   "payload_bytes_per_rank_per_step": P, "pairs": pairs,
-                   "l2": "inputs larger than L2 (4.8 GB per direction per step)",
-                   "parallelism": f"{world // 2} NVLink pairs, push over CUDA IPC"},
-        "roofline": {"bound": "nvlink", "achieved": per_dir, "peak": NVLINK_PEER_GBS, "unit": "GB/s",
-                     "frac": per_dir / NVLINK_PEER_GBS, "traffic": None,
-                     "peak_source": "peer copy per direction measured on this pool (profiling recipe); 900 nominal"},
-        "e2e": {"value": world * P / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 4,
-                "api": "lmpool_b200.kv_transfer.swap_batch(host id lists)"},
-        "gpu_launches": (4 if mode == "push" else 2) * args.steps,
+        "config": line_config(g, world),
+        "roofline": {"bound": "nvlink", "achieved": per_dir, "peak": NVLINK_NOMINAL_GBS, "unit": "GB/s",
+                     "frac": per_dir / NVLINK_NOMINAL_GBS, "traffic": traffic,
+                     "traffic_kind": "NVLink bytes on the wire per push launch and direction (payload + 18.75% "
+                                     "posted-write packet overhead), from profiles/push_nvlink_pair.txt scaled by "
+                                     "blocks",
+                     "peak_source": "NVLink 5 per-direction bandwidth, 900 GB/s nominal (the north-star's figure)",
+                     "posted_write_ceiling_GB/s": NVLINK_NOMINAL_GBS / 1.1875,
+                     "frac_of_posted_write_ceiling": per_dir / (NVLINK_NOMINAL_GBS / 1.1875),
+                     "peer_copy_measured": copies,
+                     "frac_of_measured_peer_copy": (per_dir / copies["both_directions_GB/s_per_direction"])
+                     if copies else None},
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "cpu_baseline_host": cpu["host"],
+        "e2e": {"value": world * P / (e2e_in["ms_per_step"] * 1e-3) / 1e9, "unit": "GB/s",
+                "ms_per_step": e2e_in["ms_per_step"], "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 8,
+                "api": "lmpool_b200.kv_transfer.swap_in(negotiate_blocks=False), host id lists: per pair 0->1 then "
+                       "1->0 as two plans (LMPool runs one plan per pair at a time), pull mode",
+                "source_call_ms": e2e_in["source_call_ms"],
+                "swap_batch": {"value": world * P / (batch_ms * 1e-3) / 1e9, "ms_per_step": batch_ms,
+                               "api": f"lmpool_b200.kv_transfer.swap_batch (both directions at once, {mode})"}},
+        "gpu_launches": (4 if mode == "push" else 5) * args.steps,
         "transfer_mode": mode,
+        "verified_bitexact": True,
+        "verification": {"phase_a": phase_a_chk, "phase_a_untouched": [x["untouched"] for x in gathered],
+                         "after_e2e_swap_in": e2e_in_chk, "after_e2e_swap_batch": e2e_chk,
+                         "method": "every moved (plane, layer, block) chunk compared byte for byte with the bytes "
+                                   "the reference's algorithm delivers on the same GPUs (index_select -> NCCL "
+                                   "send/recv per plane and layer); untouched blocks: 64-bit per-block "
+                                   "fingerprints before and after; config 3 cases, phase B schedules and config 5 "
+                                   "verified the same way"},
         "other_mode": {"mode": other, "ms_per_step": other_ms,
-                       "GB/s_per_direction": P / (other_ms * 1e-3) / 1e9},
+                       "GB/s_per_direction": P / (other_ms * 1e-3) / 1e9,
+                       "frac_nvlink": P / (other_ms * 1e-3) / 1e9 / NVLINK_NOMINAL_GBS},
         "clocks": merge_clocks([item["clk"] for item in gathered]),
+        "reference_gpu_phase_a": ref_a,
         "pair_sweep": sweep,
         "reference_gpu_path": ref_pair,
         "phase_b": ({m: {k: v for k, v in r.items() if k != "ok"} for m, r in phase_b.items()} if phase_b else None),
+        "config5": c5,
     }
 
 
 def bench_pair_one_process(args) -> dict:
     """One process drives cuda:0 (source) and cuda:1 (destination): the pair
     protocol at Qwen3-8B geometry with launches enqueued in dependency order
-    (publish on 1, wait_armed + push on 0, wait_done on 1), so every bounded
-    wait is satisfied by a launch issued before it. Used for profiling the
-    NVLink push with one process, and as a quick pair number."""
-    from lmpool_b200 import kv_transfer as kt
+    (push: publish on 1, wait_armed + push on 0, wait_done on 1; pull:
+    request on 1, grant on 0, wait for the grant + pull on 1), so every
+    bounded wait is satisfied by a launch issued before it. Used for
+    profiling the NVLink kernels with one process, and as a quick pair number."""
     from lmpool_b200.endpoint import TransferEndpoint
     from lmpool_b200.layout import affine_layout
 
@@ -898,17 +1367,17 @@ def bench_pair_one_process(args) -> dict:
     src_t = torch.tensor(perm[:B], dtype=torch.int64, device="cuda:0")
     dst_t = torch.tensor(perm[B:2 * B], dtype=torch.int64, device="cuda:1")
     s0, s1 = torch.cuda.current_stream(0), torch.cuda.current_stream(1)
-
     src_on_1 = src_t.to("cuda:1")
-    pull_status = torch.zeros(1, dtype=torch.int32, device="cuda:1")
 
     def one():
-        if args.pull:
-            # destination-driven: cuda:1 bulk-loads the source blocks from
-            # cuda:0's cache over NVLink and stores them locally
-            kt._launch_move(1, l10.cache, eps[1].cache, src_on_1, dst_t, B, pull_status, s1)
-            return
         token = eps[1].next_token(0)
+        if args.pull:
+            eps[1].request(l10, B, token, s1)
+            eps[0].grant(l01, B, 30.0, s0)
+            eps[1].wait_done(0, token, 30.0, s1)
+            eps[1].pull(eps[1].cache, [(l10, l10.cache, src_on_1, dst_t, B, token)], s1)
+            eps[0].wait_pulled(1, 30.0, s0)
+            return
         eps[1].publish(l10, dst_t, B, token, s1)
         eps[0].wait_armed(l01, B, 30.0, s0)
         eps[0].push(eps[0].cache, [(l01, l01.cache, src_t, B)], s0)
@@ -931,8 +1400,6 @@ def bench_pair_one_process(args) -> dict:
     ms = e0.elapsed_time(e1) / args.steps
     eps[0].check_status(s0, "pair1p source")
     eps[1].check_status(s1, "pair1p destination")
-    if int(pull_status.item()):
-        raise RuntimeError(f"pull reported status {int(pull_status.item())}")
     ok = all(torch.equal(caches[1][:, :, perm[B + i]].cpu().view(torch.int16),
                          caches[0][:, :, perm[i]].cpu().view(torch.int16)) for i in (0, B - 1))
     for ep in eps:
@@ -942,23 +1409,14 @@ def bench_pair_one_process(args) -> dict:
     P = payload_bytes(g, B)
     return {"workload": "pair, one process, cuda:0 -> cuda:1, " + ("pull by cuda:1" if args.pull else "push by cuda:0"),
             "blocks": B, "cache_blocks": N, "ms_per_step": ms,
-            "GB/s": P / (ms * 1e-3) / 1e9, "frac_nvlink": P / (ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, "verified": ok}
-
-
-CONFIG5 = dict(workload="config5: 70B-like transfer (B=1024 to the NVLink partner, both directions) under "
-                        "concurrent store_kvcache (T=256 tokens x 80 layers per step)",
-               L=80, N=16384, bs=16, H=8, D=128, B=1024, T=256)
+            "GB/s": P / (ms * 1e-3) / 1e9, "frac_nvlink": P / (ms * 1e-3) / 1e9 / NVLINK_NOMINAL_GBS, "verified": ok}
 
 
 def bench_config5(args) -> dict | None:
-    """benchmark config 5 on N GPUs (pairs): the transfer alone, store_kvcache
-    alone, and both at once on two streams. The cache is shrunk from 65536 to
-    16384 blocks per rank (80 GiB; 65536 would be 320 GiB): transfer and store
-    costs depend on B and T, not on N."""
+    """``--workload config5``: config 5 alone on N GPUs (pairs)."""
     import torch.distributed as dist
 
     from lmpool_b200 import kv_transfer as kt
-    from lmpool_b200.attention import store_kvcache, store_kvcache_layers
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -966,126 +1424,43 @@ def bench_config5(args) -> dict | None:
     if world < 2 or world % 2:
         raise SystemExit("config 5 needs an even number of GPUs >= 2")
     torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     from datetime import timedelta
 
-    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    c = CONFIG5
-    cache = torch.empty((2, c["L"], c["N"], c["bs"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev)
-    gen = torch.Generator(device=dev).manual_seed(rank)
-    cache.normal_(generator=gen)
-    keys = torch.empty((c["L"], c["T"], c["H"], c["D"]), dtype=torch.bfloat16, device=dev).normal_(generator=gen)
-    values = torch.empty_like(keys).normal_(generator=gen)
-    kt.register_kv_cache(cache, c["L"])
-    pairs = [(r, r + 1) for r in range(0, world, 2)]
-    kt.prewarm_p2p_pairs(pairs, num_layers=c["L"], block_size=c["bs"], num_kv_heads=c["H"], head_dim=c["D"],
-                         num_blocks=2, dtype=torch.bfloat16, timeout_s=60)
-    partner = rank + 1 if rank % 2 == 0 else rank - 1
-    B = c["B"]
-    perm = seeded_perm(c["N"], 7000 + rank)
-    src_ids, dst_ids = perm[:B], perm[B:2 * B]          # fragmented, disjoint
-    # store_kvcache slots avoid both transfer sets (blocks being moved are
-    # locked: the model never writes them)
-    busy = torch.zeros(c["N"], dtype=torch.bool)
-    busy[src_ids] = True
-    busy[dst_ids] = True
-    free_blocks = (~busy).nonzero().flatten()
-    g = torch.Generator().manual_seed(77 + rank)
-    pick = free_blocks[torch.randperm(len(free_blocks), generator=g)[:c["T"]]]
-    slots = pick * c["bs"] + torch.randint(0, c["bs"], (c["T"],), generator=g)
-    slots[torch.rand(c["T"], generator=g) < 0.1] = -1
-    slots = slots.to(torch.int64).to(dev)
-    ep = kt._ENDPOINTS[local]
-    link = ep.get_link(partner)
-    xs = torch.cuda.Stream(dev)
-    ss = torch.cuda.Stream(dev)
-    src_t = torch.tensor(src_ids, dtype=torch.int64, device=dev)
-    dst_t = torch.tensor(dst_ids, dtype=torch.int64, device=dev)
-    P = B * c["L"] * 2 * c["bs"] * c["H"] * c["D"] * 2
-    row = c["H"] * c["D"] * 2
-    valid = int((slots >= 0).sum())
-    store_bytes = c["L"] * (2 * c["T"] * row + 2 * valid * row + c["T"] * 8)
-
-    psrc_t = torch.tensor(seeded_perm(c["N"], 7000 + partner)[:B], dtype=torch.int64, device=dev)
-
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     mode = "push" if args.pair_mode == "auto" else args.pair_mode   # both directions at once
-
-    def xfer():
-        ep.exchange(mode, ep.cache, [(partner, src_t, B)], [(partner, psrc_t, dst_t, B)], 60.0, xs)
-
-    def store_step():
-        with torch.cuda.stream(ss):
-            store_kvcache_layers(keys, values, cache, slots, c["bs"])
-
-    with torch.cuda.stream(ss):
-        for layer in range(c["L"]):   # warm the single-layer launch too
-            store_kvcache(keys[layer], values[layer], cache[0, layer], cache[1, layer], slots, c["bs"])
-    ep.status.zero_()
-    for _ in range(3):
-        xfer()
-        store_step()
-    torch.cuda.synchronize()
-
-    def timed_alone(fn, stream, reps) -> float:
-        dist.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    K = max(3, min(args.steps, 10))
-    x_ms = timed_alone(xfer, xs, K)
-    s_ms = timed_alone(store_step, ss, 200)
-    M = max(1, int(K * x_ms / s_ms))
-    # both at once: K transfers on one stream, M store steps on another, same start
-    dist.barrier()
-    torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    start.record(torch.cuda.current_stream(dev))
-    xs.wait_event(start)
-    ss.wait_event(start)
-    xe, se = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for k in range(max(K, M)):
-        if k < K:
-            xfer()
-        if k < M:
-            store_step()
-    xe.record(xs)
-    se.record(ss)
-    torch.cuda.synchronize()
-    t = torch.tensor([start.elapsed_time(xe) / K, start.elapsed_time(se) / M], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    xo_ms, so_ms = float(t[0]), float(t[1])
-    bits = int(ep.status.item())
-    oks: list = [None] * world
-    dist.all_gather_object(oks, bits == 0)
-    kt.check_device_status(local)
-    kt.shutdown()
+    res = config5_leg(kt, rank, world, dist, args.steps, mode)
     dist.barrier()
     dist.destroy_process_group()
     if rank != 0:
         return None
-    if not all(oks):
-        raise RuntimeError("config 5 transfer reported a device error")
-    return {
-        "metric": METRIC, "workload": c["workload"], "n_gpus": world, "unit": "GB/s",
-        "config": {k: c[k] for k in ("L", "N", "bs", "H", "D", "B", "T")},
-        "substitution": "num_blocks 65536 -> 16384 per rank (320 GiB does not fit one B200)",
-        "transfer_alone": {"ms": x_ms, "GB/s_per_direction": P / (x_ms * 1e-3) / 1e9,
-                           "frac_nvlink": P / (x_ms * 1e-3) / 1e9 / NVLINK_PEER_GBS},
-        "store_alone": {"ms_per_step": s_ms, "GB/s": store_bytes / (s_ms * 1e-3) / 1e9,
-                        "launch": "all 80 layers in one launch"},
-        "overlapped": {"transfers": K, "store_steps": M, "transfer_ms": xo_ms,
-                       "transfer_GB/s_per_direction": P / (xo_ms * 1e-3) / 1e9,
-                       "store_ms_per_step": so_ms, "store_GB/s": store_bytes / (so_ms * 1e-3) / 1e9},
-        "payload_bytes_per_direction": P, "store_bytes_per_step": store_bytes, "transfer_mode": mode,
-    }
+    if not res["verified_bitexact"]:
+        raise RuntimeError("config 5 verification failed")
+    return dict(res, metric=METRIC, n_gpus=world, unit="GB/s")
+
+
+def reference_arm(args, rank: int) -> None:
+    """``--impl reference``: the reference's CPU path on this host's cores, on
+    the same workload, metric and config as the B200 arm (rank 0 only)."""
+    if rank != 0:
+        return
+    world = max(1, args.gpus)
+    g = LOCAL if world <= 1 else PAIRS
+    if world <= 1:
+        res = cpu_baseline_local(g, CPU_SAMPLE_BLOCKS, seconds=min(20.0, 2.0 * max(1, args.steps)))
+        note = ("pack + unpack with the reference's torch ops in one process (the 1-GPU workload is a local move; "
+                "no transport between pack and unpack)")
+    else:
+        res = cpu_baseline_gloo(g, CPU_SAMPLE_BLOCKS, both_ways=True, seconds=min(20.0, 2.0 * max(1, args.steps)))
+        note = "one pair over gloo on the host cores, both directions (more pairs would share the same cores)"
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": res["steps"], "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic bf16 N(0,1) KV caches, seeded randperm block ids",
+            "config": line_config(g, world),
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline_host": res["host"], "note": note,
+            "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 def main() -> None:
@@ -1113,19 +1488,7 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
 
     if args.impl == "reference":
-        if rank != 0:
-            return
-        g = LOCAL if args.gpus <= 1 else PAIRS
-        res = cpu_reference(g, CPU_SAMPLE_BLOCKS, steps=args.steps, warmup=args.warmup)
-        line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
-                "steps": res["steps"], "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic bf16 KV cache, seeded randperm block ids",
-                "config": {"workload": g["workload"], "num_layers": g["L"], "block_size": g["bs"],
-                           "num_kv_heads": g["H"], "head_dim": g["D"], "blocks_per_step": CPU_SAMPLE_BLOCKS},
-                "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
-                "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        reference_arm(args, rank)
         return
 
     from lmpool_b200 import _capi
@@ -1139,7 +1502,7 @@ def main() -> None:
         res = bench_pair_one_process(args)
     elif args.workload == "store":
         torch.cuda.set_device(0)
-        res = bench_store_kvcache(0, hbm_peak()[0], num_blocks=args.cache_blocks)
+        res = bench_store_kvcache(0, hbm_peak()[0], iters=max(3, args.steps), num_blocks=args.cache_blocks)
     elif world > 1 or args.gpus > 1:
         res = bench_pairs(args)
     else:

@@ -8,9 +8,11 @@
  *   -------------------------------------------------  ------------------------------
  *   kv_transfer.py:229-248 _pack_all_layer_blocks      kvx_move_blocks (dst = payload)
  *   kv_transfer.py:264-276 _unpack_all_layer_blocks    kvx_move_blocks (src = payload)
- *   kv_transfer.py:395-475 swap_in (planned path,      pull (default): kvx_pair_pull
- *     negotiate_blocks=False): index_select ->           (destination), kvx_pair_wait_pulled
- *     NCCL send/recv -> index_copy_                      (source); push: kvx_pair_publish +
+ *   kv_transfer.py:395-475 swap_in (planned path,      pull (default): kvx_pair_request +
+ *     negotiate_blocks=False): index_select ->           kvx_pair_wait_done + kvx_pair_pull
+ *     NCCL send/recv -> index_copy_                      (destination), kvx_pair_grant
+ *                                                        [+ kvx_pair_wait_pulled] (source);
+ *                                                        push: kvx_pair_publish +
  *                                                        kvx_pair_wait_done (destination),
  *                                                        kvx_pair_wait_armed + kvx_pair_push
  *                                                        (source)
@@ -50,7 +52,7 @@
 extern "C" {
 #endif
 
-#define KVX_ABI_VERSION 1
+#define KVX_ABI_VERSION 2
 
 /* ---- host status codes ------------------------------------------------- */
 #define KVX_OK 0
@@ -119,6 +121,8 @@ typedef struct kvx_tuning {
     int32_t ctas_per_sm;   /* 0 = automatic */
     int32_t tile_bytes;    /* 0 = automatic; else multiple of 16 */
     int32_t stages;        /* TMA ring depth; 0 = automatic */
+    int32_t store_pdl;     /* store_kvcache launch: 0 = automatic (programmatic dependent launch), 1 = on, 2 = off */
+    int32_t reserved;      /* must be 0 */
 } kvx_tuning;
 
 /* ---- library ------------------------------------------------------------ */
@@ -193,20 +197,43 @@ int kvx_pair_push(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* 
  * Same replacement of swap_in (kv_transfer.py:395-475), driven by the
  * destination, which already holds both id lists (execute_swap_in receives
  * the source ids and its reserved targets, model_runner.py:777-806). The
- * source's blocks are locked from prepare to finalize, so no handshake
- * precedes the copy:
+ * reference's source packs on its own stream after all earlier work
+ * (kv_transfer.py:463-466), so its blocks are read only once the source's
+ * own writes to them are done; the grant keeps that ordering:
+ *   kvx_pair_request     (destination) posts the block count (tagged as a
+ *                        pull) and the arm token into the source's mailbox.
+ *   kvx_pair_grant       (source) waits (bounded) for an arm newer than the
+ *                        last one consumed from that destination, checks the
+ *                        count, and release-stores the token into the
+ *                        destination's done[src] flag (token | FAIL on a
+ *                        count mismatch). Enqueued on the source's stream, it
+ *                        runs after every earlier kernel there, so blocks the
+ *                        source was still writing are complete before the
+ *                        destination can see the grant.
+ *   kvx_pair_wait_done   (destination) waits (bounded) for the grant.
  *   kvx_pair_pull        (destination) one launch reading every source's
  *                        chunks from its cache over NVLink with bulk copies
- *                        and storing them into the local reserved blocks;
- *                        the last CTA per source release-stores that
- *                        source's token into the source's `pulled` flag.
- *                        The data is in place when the launch completes.
- *   kvx_pair_wait_pulled (source) waits (bounded) until the destination
- *                        reports a pull newer than the last one consumed, so
- *                        execute_swap_out returns once its blocks are read.
+ *                        and storing them into the local reserved blocks. A
+ *                        source's segment copies only if done[src] equals
+ *                        that source's token when the launch starts (else it
+ *                        copies nothing). The last CTA per source
+ *                        release-stores the token (token | FAIL if the
+ *                        segment did not copy or a CTA failed) into the
+ *                        source's `pulled` flag. The data is in place when
+ *                        the launch completes.
+ *   kvx_pair_wait_pulled (source, optional) waits (bounded) until the
+ *                        destination reports a pull newer than the last one
+ *                        consumed; FAIL -> KVX_DEV_PEER_FAILED.
+ * A push arm and a pull request never satisfy each other (the count words
+ * differ), so two ends that disagree on the mode fail instead of moving data.
  * Measured on B200 at Qwen3-8B geometry, B=64: 777 GB/s per direction for
  * pull against 713 GB/s for push (NVLink reads carry less packet overhead
  * than posted writes). */
+int kvx_pair_request(int32_t device, const kvx_mailbox* src_mailbox_mapped, int32_t my_rank, int64_t num_ids,
+                     uint64_t token, void* stream);
+int kvx_pair_grant(int32_t device, const kvx_mailbox* my_mailbox, const kvx_mailbox* dst_mailbox_mapped,
+                   int32_t my_rank, int32_t dst_rank, int64_t num_ids, uint64_t timeout_ns, int32_t* status_dev,
+                   void* stream);
 int kvx_pair_pull(int32_t device, const kvx_cache_desc* dst, const kvx_mailbox* my_mailbox, int32_t my_rank,
                   const kvx_pull_source* sources, int32_t num_sources, int32_t* status_dev, void* stream);
 int kvx_pair_wait_pulled(int32_t device, const kvx_mailbox* my_mailbox, int32_t dst_rank, uint64_t timeout_ns,
@@ -233,10 +260,11 @@ int kvx_pair_wait_pulled(int32_t device, const kvx_mailbox* my_mailbox, int32_t 
  *     rejected with KVX_EINVAL.
  *   - The first call on a device resolves the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
- *   - Every call shares the array. Each call clears its destinations'
- *     counters on `stream` before launching, so calls that overlap on the GPU
- *     (two streams pushing to the same destination rank at once) race and
- *     must not be issued.
+ *   - Every call shares the array, one counter per destination rank. Each
+ *     call clears its destinations' counters on `stream` before launching,
+ *     so any two calls on the same device whose pushes to one destination
+ *     rank overlap on the GPU race and must not be issued: two streams of one
+ *     caller, or two callers acting as different source ranks on one GPU.
  */
 #define KVX_NOALLOC_MAX_PEERS 64
 int kvx_pair_push_noalloc(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* my_mailbox,
@@ -251,6 +279,12 @@ int kvx_mailbox_create(int32_t device, int32_t max_peers, int64_t max_blocks, kv
 int kvx_mailbox_destroy(int32_t device, const kvx_mailbox* mailbox);
 /* Last completion token this rank received from `src_rank` (host read). */
 int kvx_mailbox_read_done(int32_t device, const kvx_mailbox* mailbox, int32_t src_rank, uint64_t* token_out);
+/* Zero every word of `peer`'s pair state in this rank's own mailbox (arm,
+ * count, done, consumed, go, pulled and both CTA counters), enqueued on
+ * `stream`. Both ranks of a pair call it, with no transfer of that pair in
+ * flight, before they start again from token 1: how a pair disabled after a
+ * timeout is brought back without recreating the mailbox (prewarm does it). */
+int kvx_mailbox_reset_peer(int32_t device, const kvx_mailbox* mailbox, int32_t peer, void* stream);
 
 /* Export the allocation holding dev_ptr: 64-byte cudaIpcMemHandle_t plus the
  * byte offset of dev_ptr inside that allocation. */

@@ -16,7 +16,7 @@ import threading
 from pathlib import Path
 
 _LIB_PATH = Path(__file__).resolve().parent / "_kvx.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 KVX_OK = 0
 KVX_EINVAL = 1
@@ -115,6 +115,8 @@ class Tuning(ctypes.Structure):
         ("ctas_per_sm", ctypes.c_int32),
         ("tile_bytes", ctypes.c_int32),
         ("stages", ctypes.c_int32),
+        ("store_pdl", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -142,6 +144,8 @@ SIGNATURES: dict[str, tuple] = {
     "kvx_pair_wait_done": (_i32, [_i32, _P(Mailbox), _i32, _u64, _u64, _vp, _vp]),
     "kvx_pair_wait_armed": (_i32, [_i32, _P(Mailbox), _P(Mailbox), _i32, _i32, _i64, _u64, _vp, _vp]),
     "kvx_pair_push": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PushTarget), _i32, _vp, _vp]),
+    "kvx_pair_request": (_i32, [_i32, _P(Mailbox), _i32, _i64, _u64, _vp]),
+    "kvx_pair_grant": (_i32, [_i32, _P(Mailbox), _P(Mailbox), _i32, _i32, _i64, _u64, _vp, _vp]),
     "kvx_pair_pull": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PullSource), _i32, _vp, _vp]),
     "kvx_pair_wait_pulled": (_i32, [_i32, _P(Mailbox), _i32, _u64, _vp, _vp]),
     "kvx_pair_push_noalloc": (_i32, [_i32, _P(CacheDesc), _P(Mailbox), _i32, _P(PushTarget), _i32, _vp, _vp]),
@@ -149,6 +153,7 @@ SIGNATURES: dict[str, tuple] = {
     "kvx_mailbox_create": (_i32, [_i32, _i32, _i64, _P(Mailbox)]),
     "kvx_mailbox_destroy": (_i32, [_i32, _P(Mailbox)]),
     "kvx_mailbox_read_done": (_i32, [_i32, _P(Mailbox), _i32, _P(_u64)]),
+    "kvx_mailbox_reset_peer": (_i32, [_i32, _P(Mailbox), _i32, _vp]),
     "kvx_ipc_export": (_i32, [_i32, _vp, _vp, _P(_u64)]),
     "kvx_ipc_open": (_i32, [_i32, _vp, _u64, _P(_u64)]),
     "kvx_ipc_close": (_i32, [_i32, _u64, _u64]),

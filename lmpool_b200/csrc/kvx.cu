@@ -43,12 +43,17 @@ namespace kvx {
 constexpr int kMaxSegments = 8;
 constexpr int kRegThreads = 256;
 constexpr int kRegUnroll = 4;
-constexpr int kStoreThreads = 256;
+constexpr int kStoreThreads = 64;   // one token's K row and V row per CTA
 constexpr int kMaxDevices = 64;
 constexpr uint64_t kFailBit = 1ull << 63;
 // Upper bound on mbarrier polls of a bulk-copy stage before the pipeline
 // gives up (each poll may suspend for a hardware-chosen interval).
 constexpr uint32_t kMaxPipePolls = 1u << 24;
+// Segment completion counters count CTAs in the low 16 bits and failed CTAs
+// in the high 16 bits (a grid never exceeds 148 SMs x 32 CTAs < 2^16).
+constexpr unsigned kCtaOne = 1u;
+constexpr unsigned kCtaFailed = 1u << 16;
+constexpr unsigned kCtaMask = kCtaFailed - 1u;
 
 struct SegParams {
     uint64_t dst_base;
@@ -61,6 +66,10 @@ struct SegParams {
     int64_t num_ids;
     int64_t num_tiles;
     const uint64_t* go;      // nullptr: always run; else run iff *go != 0 and signal *go
+    // Grant check (pull): the segment copies only if *cond == cond_value when
+    // it starts; otherwise it moves nothing and signals token | FAIL.
+    const uint64_t* cond;
+    uint64_t cond_value;
     unsigned int* counter;   // CTA completion counter (nullptr: no signal)
     uint64_t* flag;          // completion flag written by the segment's last CTA
     uint64_t token;          // token to signal when go is nullptr (pull)
@@ -155,20 +164,26 @@ __device__ __forceinline__ void copy_span(char* __restrict__ dst, const char* __
     for (; i < n; i += stride) st_stream(d + i, ld_stream(s + i));
 }
 
-// Completion of one segment: every CTA of the segment counts itself in; the
-// last one makes the whole segment's stores visible system-wide and
-// release-stores the token into the destination's flag.
-__device__ __forceinline__ void finish_segment_cta(const SegParams& g, uint64_t token) {
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(g.counter, 1u);
-        if (prev == static_cast<unsigned>(g.cta_count) - 1u) {
-            __threadfence_system();
-            st_release_sys(g.flag, token);
-            atomicExch(g.counter, 0u);
-        }
+// Completion of one segment, called by one thread per CTA after the CTA's
+// stores are fenced: every CTA counts itself in, failed or not; the last one
+// release-stores the token into the flag (token | FAIL when any CTA of the
+// segment failed or skipped its copy) and re-arms the counter, so a failure
+// never leaves the counter part-way for the next transfer.
+__device__ __forceinline__ void count_segment_cta(const SegParams& g, uint64_t token, bool failed) {
+    const unsigned mine = kCtaOne + (failed ? kCtaFailed : 0u);
+    const unsigned prev = atomicAdd(g.counter, mine);
+    if ((prev & kCtaMask) == static_cast<unsigned>(g.cta_count) - 1u) {
+        const bool any_failed = ((prev + mine) >> 16) != 0u;
+        __threadfence_system();
+        st_release_sys(g.flag, any_failed ? (token | kFailBit) : token);
+        atomicExch(g.counter, 0u);
     }
+}
+
+// Whether the segment may copy: its grant word (pull) must carry exactly the
+// token this transfer was granted under.
+__device__ __forceinline__ bool segment_granted(const SegParams& g) {
+    return g.cond == nullptr || ld_acquire_sys(g.cond) == g.cond_value;
 }
 
 template <int VEC>
@@ -180,13 +195,21 @@ __global__ void __launch_bounds__(kRegThreads) move_reg_kernel(const __grid_cons
         token = ld_relaxed_gpu(g.go);
         if (token == 0) return;  // the arm wait failed: this segment does not run
     }
+    __shared__ int granted;
+    if (threadIdx.x == 0) granted = segment_granted(g) ? 1 : 0;
+    __syncthreads();
     const int64_t local = static_cast<int64_t>(blockIdx.x) - g.cta_begin;
-    for (int64_t t = local; t < g.num_tiles; t += g.cta_count) {
-        const TileAddr a = decode_tile(p, g, t, threadIdx.x == 0);
-        if (!a.ok) continue;
-        copy_span<VEC>(a.dst, a.src, a.len);
+    if (granted) {
+        for (int64_t t = local; t < g.num_tiles; t += g.cta_count) {
+            const TileAddr a = decode_tile(p, g, t, threadIdx.x == 0);
+            if (!a.ok) continue;
+            copy_span<VEC>(a.dst, a.src, a.len);
+        }
     }
-    if (g.counter != nullptr) finish_segment_cta(g, token);
+    if (g.counter == nullptr) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) count_segment_cta(g, token, !granted);
 }
 
 // Bulk-copy engine: one warp per CTA, lane 0 issues everything. STAGES ring
@@ -206,11 +229,13 @@ __global__ void __launch_bounds__(32) move_bulk_kernel(const __grid_constant__ M
         token = ld_relaxed_gpu(g.go);
         if (token == 0) return;
     }
+    const bool granted = segment_granted(g);
     for (int k = 0; k < STAGES; ++k) mbar_init(&bars[k], 1);
     mbar_init_fence();
 
     const int64_t local = static_cast<int64_t>(blockIdx.x) - g.cta_begin;
-    const int64_t ntiles = (local < g.num_tiles) ? (g.num_tiles - 1 - local) / g.cta_count + 1 : 0;
+    const int64_t ntiles =
+        (granted && local < g.num_tiles) ? (g.num_tiles - 1 - local) / g.cta_count + 1 : 0;
     char* dst_of[STAGES];
     uint32_t len_of[STAGES];
     bool ok_of[STAGES];
@@ -252,21 +277,26 @@ __global__ void __launch_bounds__(32) move_bulk_kernel(const __grid_constant__ M
         if (!ready) {
             atomicOr(p.status, KVX_DEV_PIPE_TIMEOUT);
             failed = true;
+            // Loads of tiles k .. k + kAhead may still be in flight into this
+            // CTA's shared memory: give each a second bounded wait before the
+            // CTA leaves, so none lands after it exits.
+            const int64_t last = (k + kAhead + 1 < ntiles ? k + kAhead + 1 : ntiles);
+            for (int64_t kk = k; kk < last; ++kk) {
+                const int sk = static_cast<int>(kk % STAGES);
+                const uint32_t pk = static_cast<uint32_t>((kk / STAGES) & 1);
+                for (uint32_t poll = 0; poll < kMaxPipePolls && !mbar_try_wait(&bars[sk], pk); ++poll) {
+                }
+            }
             break;
         }
         if (ok_of[st]) bulk_store(dst_of[st], ring + static_cast<int64_t>(st) * p.tile_bytes, len_of[st]);
         bulk_commit();
     }
     bulk_wait_all();
-    if (failed || g.counter == nullptr) return;
+    if (g.counter == nullptr) return;
     fence_proxy_async();
     __threadfence_system();
-    const unsigned prev = atomicAdd(g.counter, 1u);
-    if (prev == static_cast<unsigned>(g.cta_count) - 1u) {
-        __threadfence_system();
-        st_release_sys(g.flag, token);
-        atomicExch(g.counter, 0u);
-    }
+    count_segment_cta(g, token, failed || !granted);
 }
 
 // ---------------------------------------------------------------------------
@@ -298,23 +328,37 @@ __host__ __device__ inline MailboxLayout mailbox_layout(int64_t peers, int64_t m
     return m;
 }
 
-// Destination -> source mailbox: target ids, their count, then the arm token.
+// A pull request posts its block count with this tag, so that a source
+// expecting a push (which needs target ids in its mailbox) and a source
+// expecting a pull never accept each other's arm: the counts differ.
+constexpr uint64_t kPullTag = 1ull << 62;
+
+// Destination -> source mailbox: `n` target ids (push; none for a pull
+// request), the count word, then the arm token.
 __global__ void __launch_bounds__(1024) publish_kernel(const int64_t* ids, int64_t n, int64_t* remote_ids,
-                                                         uint64_t* remote_count, uint64_t* remote_arm, uint64_t token) {
+                                                         uint64_t count_word, uint64_t* remote_count,
+                                                         uint64_t* remote_arm, uint64_t token) {
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) remote_ids[i] = ids[i];
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-        st_relaxed_sys(remote_count, static_cast<uint64_t>(n));
+        st_relaxed_sys(remote_count, count_word);
         __threadfence_system();
         st_release_sys(remote_arm, token);
     }
 }
 
 // Source: wait for an arm newer than the last one consumed from this
-// destination; check the posted count; record the token the push will signal.
+// destination and check the posted count word.
+//   push (go != nullptr): record the token the push will signal in *go
+//     (0 = do not run); a count mismatch answers token | FAIL in remote_done.
+//   grant (go == nullptr): answer the token itself in remote_done. The store
+//     is ordered after every earlier kernel of this stream (they completed
+//     before this one started, and the fence makes their writes visible to
+//     the system), so the destination reads the blocks only after the
+//     source's own writes to them.
 __global__ void wait_armed_kernel(const uint64_t* arm, const uint64_t* count, uint64_t* consumed, uint64_t* go,
-                                  uint64_t* remote_done, int64_t expected_count, uint64_t timeout_ns,
+                                  uint64_t* remote_done, uint64_t expected_count, uint64_t timeout_ns,
                                   int32_t* status) {
     if (threadIdx.x != 0) return;
     const uint64_t last = ld_relaxed_gpu(consumed);
@@ -326,13 +370,16 @@ __global__ void wait_armed_kernel(const uint64_t* arm, const uint64_t* count, ui
         if (v > last && (v & kFailBit) == 0) {
             const uint64_t n = ld_acquire_sys(count);
             *consumed = v;
-            if (n != static_cast<uint64_t>(expected_count)) {
+            if (n != expected_count) {
                 atomicOr(status, KVX_DEV_COUNT_MISMATCH);
-                *go = 0;
+                if (go != nullptr) *go = 0;
                 __threadfence_system();
                 st_release_sys(remote_done, v | kFailBit);
-            } else {
+            } else if (go != nullptr) {
                 *go = v;
+            } else {
+                __threadfence_system();
+                st_release_sys(remote_done, v);
             }
             __threadfence();
             return;
@@ -340,7 +387,7 @@ __global__ void wait_armed_kernel(const uint64_t* arm, const uint64_t* count, ui
         if (global_timer_ns() - t0 > timeout_ns) break;
         __nanosleep(128);
     }
-    *go = 0;
+    if (go != nullptr) *go = 0;
     __threadfence();
     atomicOr(status, KVX_DEV_TIMEOUT);
 }
@@ -420,16 +467,37 @@ struct StoreParams {
     int32_t* status;
 };
 
+// One warp per (token, plane), both planes of a token in one CTA, grid.y =
+// layer. The token's row (up to 4 x 32 x VEC bytes; 2 KiB at H=8, D=128,
+// VEC=16) is loaded before the slot id is tested, so the slot load and the
+// row loads are in flight together; rows longer than that take a second loop.
+// Launched with programmatic stream serialization: the slot id (an input of
+// the whole step, written before the forward starts) is read before
+// griddepcontrol.wait, K/V and the cache only after it, so everything the
+// previous kernel wrote is visible; launch_dependents lets the next kernel
+// (the next layer's store, when it uses the same launch) start its own
+// prologue early. Without the launch attribute both instructions are no-ops.
 template <int VEC>
 __global__ void __launch_bounds__(kStoreThreads) store_kvcache_kernel(const __grid_constant__ StoreParams p) {
     using V = typename VecT<VEC>::T;
+    constexpr int kUnroll = 4;
+    griddep_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int64_t w = static_cast<int64_t>(blockIdx.x) * (kStoreThreads / 32) + (threadIdx.x >> 5);
     const int64_t t = w >> 1;
     const int kv = static_cast<int>(w & 1);
     if (t >= p.num_tokens) return;
     const int64_t layer = blockIdx.y;
-    const int64_t slot = __ldg(p.slots + t);
+    const int64_t slot = ld_cg(p.slots + t);
+    griddep_wait();
+    const char* src = kv ? p.value + layer * p.value_layer_stride + t * p.value_token_stride
+                         : p.key + layer * p.key_layer_stride + t * p.key_token_stride;
+    const V* s = reinterpret_cast<const V*>(src);
+    const int64_t n = p.row_bytes / VEC;
+    V r[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+        if (lane + 32 * k < n) r[k] = ld_cg(s + lane + 32 * k);
     if (slot == -1) return;  // padding token (attention.py:29-30)
     if (slot < -1 || slot >= p.num_slots) {
         if (lane == 0 && kv == 0) atomicOr(p.status, KVX_DEV_BAD_SLOT);
@@ -437,22 +505,13 @@ __global__ void __launch_bounds__(kStoreThreads) store_kvcache_kernel(const __gr
     }
     const int64_t blk = slot / p.block_size;
     const int64_t off = slot - blk * p.block_size;
-    const char* src = kv ? p.value + layer * p.value_layer_stride + t * p.value_token_stride
-                         : p.key + layer * p.key_layer_stride + t * p.key_token_stride;
     char* dst = (kv ? p.v_cache + layer * p.vc_layer_stride : p.k_cache + layer * p.kc_layer_stride) +
                 blk * p.block_stride + off * p.slot_stride;
-    const V* s = reinterpret_cast<const V*>(src);
     V* d = reinterpret_cast<V*>(dst);
-    const int64_t n = p.row_bytes / VEC;
-    int64_t i = lane;
-    for (; i + 3 * 32 < n; i += 4 * 32) {
-        V r0 = ld_stream(s + i), r1 = ld_stream(s + i + 32), r2 = ld_stream(s + i + 64), r3 = ld_stream(s + i + 96);
-        d[i] = r0;
-        d[i + 32] = r1;
-        d[i + 64] = r2;
-        d[i + 96] = r3;
-    }
-    for (; i < n; i += 32) d[i] = ld_stream(s + i);
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+        if (lane + 32 * k < n) d[lane + 32 * k] = r[k];
+    for (int64_t i = lane + 32 * kUnroll; i < n; i += 32) d[i] = ld_cg(s + i);
 }
 
 // ---------------------------------------------------------------------------
@@ -500,7 +559,7 @@ struct DeviceGuard {
     if (guard_.err != cudaSuccess) return cuda_fail(guard_.err, "select device")
 
 std::mutex g_mu;
-kvx_tuning g_tuning = {0, 0, 0, 0};
+kvx_tuning g_tuning = {0, 0, 0, 0, 0, 0};
 int g_sm_count[kMaxDevices] = {0};
 bool g_bulk_attr_set[kMaxDevices][4] = {};
 
@@ -730,6 +789,8 @@ int kvx_set_tuning(const kvx_tuning* t) {
     if (t->tile_bytes < 0 || (t->tile_bytes % 16) != 0) return fail(KVX_EINVAL, "tile_bytes must be a multiple of 16");
     if (t->stages != 0 && t->stages != 4 && t->stages != 6 && t->stages != 8 && t->stages != 12)
         return fail(KVX_EINVAL, "stages must be 0, 4, 6, 8 or 12");
+    if (t->store_pdl < 0 || t->store_pdl > 2) return fail(KVX_EINVAL, "store_pdl must be 0, 1 or 2");
+    if (t->reserved != 0) return fail(KVX_EINVAL, "reserved must be 0");
     std::lock_guard<std::mutex> lk(g_mu);
     g_tuning = *t;
     return KVX_OK;
@@ -927,8 +988,8 @@ int kvx_pair_publish(int32_t device, const kvx_mailbox* src_mb, int32_t my_rank,
     const MailboxLayout m = mailbox_layout(src_mb->max_peers, src_mb->max_blocks);
     int64_t* ids = mb_ptr<int64_t>(src_mb, m.ids, static_cast<int64_t>(my_rank) * src_mb->max_blocks);
     publish_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-        dst_ids_dev, num_ids, ids, mb_ptr<uint64_t>(src_mb, m.count, my_rank), mb_ptr<uint64_t>(src_mb, m.arm, my_rank),
-        token);
+        dst_ids_dev, num_ids, ids, static_cast<uint64_t>(num_ids), mb_ptr<uint64_t>(src_mb, m.count, my_rank),
+        mb_ptr<uint64_t>(src_mb, m.arm, my_rank), token);
     KVX_CUDA(cudaGetLastError(), "launch publish kernel");
     return KVX_OK;
 }
@@ -962,8 +1023,64 @@ int kvx_pair_wait_armed(int32_t device, const kvx_mailbox* my_mb, const kvx_mail
     wait_armed_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
         mb_ptr<uint64_t>(my_mb, m.arm, dst_rank), mb_ptr<uint64_t>(my_mb, m.count, dst_rank),
         mb_ptr<uint64_t>(my_mb, m.consumed, dst_rank), mb_ptr<uint64_t>(my_mb, m.go, dst_rank),
-        mb_ptr<uint64_t>(dst_mb, md.done, my_rank), num_ids, timeout_ns, status_dev);
+        mb_ptr<uint64_t>(dst_mb, md.done, my_rank), static_cast<uint64_t>(num_ids), timeout_ns, status_dev);
     KVX_CUDA(cudaGetLastError(), "launch wait-armed kernel");
+    return KVX_OK;
+}
+
+int kvx_pair_request(int32_t device, const kvx_mailbox* src_mb, int32_t my_rank, int64_t num_ids, uint64_t token,
+                     void* stream) {
+    int rc = check_mailbox(src_mb, "source");
+    if (rc) return rc;
+    if (my_rank < 0 || my_rank >= src_mb->max_peers) return fail(KVX_EINVAL, "my_rank out of range");
+    if (num_ids < 0 || num_ids > src_mb->max_blocks)
+        return fail(KVX_EINVAL, "%lld blocks exceed the source mailbox capacity %lld", (long long)num_ids,
+                    (long long)src_mb->max_blocks);
+    if (token == 0 || (token & kFailBit)) return fail(KVX_EINVAL, "token must be in [1, 2^63)");
+    KVX_DEVICE_GUARD(device);
+    const MailboxLayout m = mailbox_layout(src_mb->max_peers, src_mb->max_blocks);
+    publish_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        nullptr, 0, nullptr, static_cast<uint64_t>(num_ids) | kPullTag, mb_ptr<uint64_t>(src_mb, m.count, my_rank),
+        mb_ptr<uint64_t>(src_mb, m.arm, my_rank), token);
+    KVX_CUDA(cudaGetLastError(), "launch request kernel");
+    return KVX_OK;
+}
+
+int kvx_pair_grant(int32_t device, const kvx_mailbox* my_mb, const kvx_mailbox* dst_mb, int32_t my_rank,
+                   int32_t dst_rank, int64_t num_ids, uint64_t timeout_ns, int32_t* status_dev, void* stream) {
+    int rc = check_mailbox(my_mb, "local");
+    if (rc) return rc;
+    rc = check_mailbox(dst_mb, "destination");
+    if (rc) return rc;
+    if (dst_rank < 0 || dst_rank >= my_mb->max_peers) return fail(KVX_EINVAL, "dst_rank out of range");
+    if (my_rank < 0 || my_rank >= dst_mb->max_peers) return fail(KVX_EINVAL, "my_rank out of range");
+    if (num_ids < 0) return fail(KVX_EINVAL, "negative block count");
+    if (status_dev == nullptr) return fail(KVX_EINVAL, "status_dev is NULL");
+    KVX_DEVICE_GUARD(device);
+    const MailboxLayout m = mailbox_layout(my_mb->max_peers, my_mb->max_blocks);
+    const MailboxLayout md = mailbox_layout(dst_mb->max_peers, dst_mb->max_blocks);
+    wait_armed_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        mb_ptr<uint64_t>(my_mb, m.arm, dst_rank), mb_ptr<uint64_t>(my_mb, m.count, dst_rank),
+        mb_ptr<uint64_t>(my_mb, m.consumed, dst_rank), nullptr, mb_ptr<uint64_t>(dst_mb, md.done, my_rank),
+        static_cast<uint64_t>(num_ids) | kPullTag, timeout_ns, status_dev);
+    KVX_CUDA(cudaGetLastError(), "launch grant kernel");
+    return KVX_OK;
+}
+
+int kvx_mailbox_reset_peer(int32_t device, const kvx_mailbox* mailbox, int32_t peer, void* stream) {
+    int rc = check_mailbox(mailbox, "local");
+    if (rc) return rc;
+    if (peer < 0 || peer >= mailbox->max_peers) return fail(KVX_EINVAL, "peer out of range");
+    KVX_DEVICE_GUARD(device);
+    const MailboxLayout m = mailbox_layout(mailbox->max_peers, mailbox->max_blocks);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint64_t words[] = {m.arm, m.done, m.count, m.consumed, m.go, m.pulled, m.pull_consumed};
+    for (uint64_t off : words)
+        KVX_CUDA(cudaMemsetAsync(mb_ptr<uint64_t>(mailbox, off, peer), 0, sizeof(uint64_t), st), "reset mailbox");
+    KVX_CUDA(cudaMemsetAsync(mb_ptr<unsigned int>(mailbox, m.counter, peer), 0, sizeof(unsigned int), st),
+             "reset mailbox");
+    KVX_CUDA(cudaMemsetAsync(mb_ptr<unsigned int>(mailbox, m.pull_counter, peer), 0, sizeof(unsigned int), st),
+             "reset mailbox");
     return KVX_OK;
 }
 
@@ -1246,6 +1363,10 @@ int kvx_pair_pull(int32_t device, const kvx_cache_desc* dst, const kvx_mailbox* 
         if (src.num_ids == 0) g.num_ids = 1;
         g.go = nullptr;
         g.token = src.token;
+        // Copy only under the source's grant of exactly this token
+        // (kvx_pair_grant answered it into done[src_rank]).
+        g.cond = mb_ptr<uint64_t>(my_mb, m.done, src.src_rank);
+        g.cond_value = src.token;
         g.counter = mb_ptr<unsigned int>(my_mb, m.pull_counter, src.src_rank);
         g.flag = mb_ptr<uint64_t>(&src.src_mailbox, ms.pulled, my_rank);
     }
@@ -1384,15 +1505,33 @@ static int store_common(int32_t device, int32_t num_layers, const void* key, con
     const int64_t blocks = (warps + wpc - 1) / wpc;
     if (blocks > 0x7fffffff) return fail(KVX_EINVAL, "too many tokens");
     const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(num_layers));
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    switch (vec) {
-        case 16: store_kvcache_kernel<16><<<grid, kStoreThreads, 0, s>>>(p); break;
-        case 8: store_kvcache_kernel<8><<<grid, kStoreThreads, 0, s>>>(p); break;
-        case 4: store_kvcache_kernel<4><<<grid, kStoreThreads, 0, s>>>(p); break;
-        case 2: store_kvcache_kernel<2><<<grid, kStoreThreads, 0, s>>>(p); break;
-        default: store_kvcache_kernel<1><<<grid, kStoreThreads, 0, s>>>(p); break;
+    int pdl;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        pdl = g_tuning.store_pdl != 2;
     }
-    KVX_CUDA(cudaGetLastError(), "launch store_kvcache kernel");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kStoreThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e;
+    switch (vec) {
+        case 16: e = cudaLaunchKernelEx(&cfg, store_kvcache_kernel<16>, p); break;
+        case 8: e = cudaLaunchKernelEx(&cfg, store_kvcache_kernel<8>, p); break;
+        case 4: e = cudaLaunchKernelEx(&cfg, store_kvcache_kernel<4>, p); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, store_kvcache_kernel<2>, p); break;
+        default: e = cudaLaunchKernelEx(&cfg, store_kvcache_kernel<1>, p); break;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(e, "launch store_kvcache kernel");
+    }
     return KVX_OK;
 }
 

@@ -61,6 +61,48 @@ __device__ __forceinline__ void st_stream(uint32_t* p, uint32_t v) { *p = v; }
 __device__ __forceinline__ void st_stream(uint16_t* p, uint16_t v) { *p = v; }
 __device__ __forceinline__ void st_stream(uint8_t* p, uint8_t v) { *p = v; }
 
+// Load cached at L2 only (never from a possibly stale L1 line): rows written
+// by the kernel just before this one, which may still have been running
+// when this one started (programmatic dependent launch).
+__device__ __forceinline__ uint4 ld_cg(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_cg(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_cg(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ld_cg(const uint16_t* p) {
+    uint16_t v;
+    asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint8_t ld_cg(const uint8_t* p) {
+    uint16_t v;
+    asm volatile("ld.global.cg.u8 %0, [%1];" : "=h"(v) : "l"(p));
+    return static_cast<uint8_t>(v);
+}
+__device__ __forceinline__ int64_t ld_cg(const int64_t* p) {
+    int64_t v;
+    asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
+
+// Programmatic dependent launch (sm_90+): let the next kernel on the stream
+// begin launching, and wait until every kernel before this one completed
+// and its memory is visible. No-ops when the launch did not opt in.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Block ids may have been written by a peer GPU (target ids posted into this
 // rank's mailbox) before this kernel started: read them at L2 (coherence
 // point for this GPU's memory), never from a possibly stale L1 line.

@@ -8,7 +8,7 @@ directed pair. It replaces the per-pair NCCL communicators of
 ``prewarm_p2p_pairs`` (src/lmpool/engine/kv_transfer.py:40-119) and the
 ``dist.send``/``dist.recv`` of ``swap_in`` (kv_transfer.py:463-470).
 
-Protocol of one transfer ``src -> dst`` (B blocks):
+Protocol of one transfer ``src -> dst`` (B blocks), push mode:
 
 =================================  ==========================================
 destination (execute_swap_in)      source (execute_swap_out)
@@ -20,6 +20,25 @@ publish: ids -> src mailbox,
 wait_done: flag == token           push: src blocks -> dst cache over NVLink;
   (bounded)                          last CTA: flag = token (release, sys)
 stream sync, status check          stream sync, status check
+=================================  ==========================================
+
+Pull mode (the default of ``swap_in``):
+
+=================================  ==========================================
+destination (execute_swap_in)      source (execute_swap_out)
+=================================  ==========================================
+token = next token for src
+request: count | PULL, arm = token
+  -> src mailbox                   grant: arm > last consumed (bounded),
+                                     count == B | PULL, then flag = token
+                                     (release, sys) on the source's stream,
+                                     after every earlier write there
+wait_done: flag == token (bounded)
+pull: src blocks over NVLink ->
+  own blocks, only if flag is
+  still token; last CTA:
+  pulled = token (| FAIL)          [wait_pulled: pulled > last consumed]
+stream sync, status check          [stream sync, status check]
 =================================  ==========================================
 
 Tokens are issued by the destination and only grow, so a late or repeated
@@ -255,6 +274,94 @@ class TransferEndpoint:
                                                 ctypes.c_void_p(_capi.stream_handle(stream))),
                     "kvx_pair_wait_done")
 
+    def request(self, link: PeerLink, num_ids: int, token: int, stream) -> None:
+        """Pull: ask the source (link.peer) to grant ``num_ids`` blocks under ``token``."""
+        self.status_clean = False
+        _capi.check(self.lib.kvx_pair_request(self.device, ctypes.byref(link.mailbox), self.rank, num_ids, token,
+                                              ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_pair_request")
+
+    def grant(self, link: PeerLink, num_ids: int, timeout_s: float | None, stream, status_ptr: int | None = None) -> None:
+        """Pull: answer the destination's request once this stream reaches here."""
+        if status_ptr is None:
+            self.status_clean = False
+            status_ptr = self.status.data_ptr()
+        _capi.check(self.lib.kvx_pair_grant(self.device, ctypes.byref(self.mailbox), ctypes.byref(link.mailbox),
+                                            self.rank, link.peer, num_ids, timeout_ns(timeout_s),
+                                            ctypes.c_void_p(status_ptr), ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_pair_grant")
+
+    # -- grants whose outcome is read later (source returns once enqueued) ---
+    ASYNC_SLOTS = 32
+
+    def grant_deferred(self, link: PeerLink, num_ids: int, timeout_s: float | None, stream, what: str) -> None:
+        """Enqueue a grant without waiting for it or for the destination's read.
+
+        The grant reports into a status word of its own; a copy of that word
+        to pinned host memory and an event follow it on ``stream``, and
+        :meth:`poll_deferred` reads the outcome once the event has completed,
+        so nothing here or later blocks on it. A failed grant disables the
+        pair (its next use raises); the destination side of the same
+        transfer fails on its own bounded wait.
+        """
+        self.poll_deferred()
+        if not hasattr(self, "_async_dev"):
+            dev = torch.device("cuda", self.device)
+            self._async_dev = torch.zeros(self.ASYNC_SLOTS, dtype=torch.int32, device=dev)
+            self._async_host = torch.zeros(self.ASYNC_SLOTS, dtype=torch.int32).pin_memory()
+            self._async_np = self._async_host.numpy()
+            self._async_free = list(range(self.ASYNC_SLOTS))
+            self._async_pending: list = []
+        if not self._async_free:            # all slots in flight: wait for the oldest
+            self._async_pending[0][1].synchronize()
+            self.poll_deferred()
+        i = self._async_free.pop()
+        word = self._async_dev[i:i + 1]
+        with torch.cuda.stream(stream):
+            word.zero_()
+            self.grant(link, num_ids, timeout_s, stream, status_ptr=word.data_ptr())
+            self._async_host[i:i + 1].copy_(word, non_blocking=True)
+            event = torch.cuda.Event()
+            event.record(stream)
+        self._async_pending.append((i, event, what, link.peer))
+
+    def poll_deferred(self, wait: bool = False) -> None:
+        """Read the outcome of deferred grants that have completed (all of
+        them when ``wait``); a failure is logged and disables its pair."""
+        pending = getattr(self, "_async_pending", None)
+        if not pending:
+            return
+        keep = []
+        for i, event, what, peer in pending:
+            if wait:
+                event.synchronize()
+            elif not event.query():
+                keep.append((i, event, what, peer))
+                continue
+            bits = int(self._async_np[i])
+            self._async_free.append(i)
+            if bits:
+                msg = f"{what}: {_capi.describe_device_status(bits)}"
+                logger.error("deferred grant failed on rank %d: %s", self.rank, msg)
+                link = self.links.get(peer)
+                if link is not None:
+                    link.poisoned = msg
+        self._async_pending = keep
+
+    def reset_pair(self, peer: int, stream) -> None:
+        """Forget every token of the pair (this rank, ``peer``): zero the pair's
+        words in this rank's mailbox and restart this side's token count.
+        Both ranks do it, with nothing of the pair in flight, before either
+        transfers again (prewarm runs it on every rank, between barriers)."""
+        _capi.check(self.lib.kvx_mailbox_reset_peer(self.device, ctypes.byref(self.mailbox), int(peer),
+                                                    ctypes.c_void_p(_capi.stream_handle(stream))),
+                    "kvx_mailbox_reset_peer")
+        with self._lock:
+            self.tokens_issued.pop(int(peer), None)
+        link = self.links.get(int(peer))
+        if link is not None:
+            link.poisoned = None
+
     def wait_armed(self, link: PeerLink, num_ids: int, timeout_s: float | None, stream) -> None:
         self.status_clean = False
         _capi.check(self.lib.kvx_pair_wait_armed(self.device, ctypes.byref(self.mailbox), ctypes.byref(link.mailbox),
@@ -312,7 +419,8 @@ class TransferEndpoint:
                     "kvx_pair_wait_pulled")
 
     def exchange(self, mode: str, local: CacheLayout, outgoing: list[tuple], incoming: list[tuple],
-                 timeout_s: float | None, stream, peer_layouts: dict | None = None) -> None:
+                 timeout_s: float | None, stream, peer_layouts: dict | None = None,
+                 wait_pulled: bool = True) -> None:
         """Enqueue every transfer of this rank (no host wait).
 
         ``outgoing`` = [(dst_rank, src ids, count)] of blocks this rank gives;
@@ -320,10 +428,12 @@ class TransferEndpoint:
         receives (src ids are used in pull mode only). ``peer_layouts`` maps a
         rank to the peer layout to read or write (default: the peer's cache).
         Push: arms for every incoming transfer first, then one push launch
-        for all outgoing ones, then the completion waits. Pull: one pull
-        launch for all incoming transfers, then the waits for the peers that
-        read this rank's blocks. Either order leaves no wait depending on a
-        later launch of any rank.
+        for all outgoing ones, then the completion waits. Pull: requests for
+        every incoming transfer first, then the grants of this rank's
+        outgoing blocks, then the waits for the incoming grants and one pull
+        launch for all incoming transfers, then (``wait_pulled``) the waits
+        for the peers that read this rank's blocks. Either order leaves no
+        wait depending on a later launch of any rank.
         """
         self.status_clean = False
         layouts = peer_layouts or {}
@@ -346,17 +456,24 @@ class TransferEndpoint:
             sources = []
             for src_rank, sids, dids, n in incoming:
                 link = self.get_link(src_rank)
-                sources.append((link, layouts.get(src_rank, link.cache), sids, dids, n, self.next_token(src_rank)))
+                token = self.next_token(src_rank)
+                self.request(link, n, token, stream)
+                sources.append((link, layouts.get(src_rank, link.cache), sids, dids, n, token))
+            for dst_rank, _sids, n in outgoing:
+                self.grant(self.get_link(dst_rank), n, timeout_s, stream)
+            for link, _layout, _sids, _dids, _n, token in sources:
+                self.wait_done(link.peer, token, timeout_s, stream)
             if sources:
                 self.pull(local, sources, stream)
-            for dst_rank, _sids, _n in outgoing:
-                self.get_link(dst_rank)
-                self.wait_pulled(dst_rank, timeout_s, stream)
+            if wait_pulled:
+                for dst_rank, _sids, _n in outgoing:
+                    self.wait_pulled(dst_rank, timeout_s, stream)
         else:
             raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull' or 'push'")
 
     def exchange_rotated(self, mode: str, local: CacheLayout, outgoing: list[tuple], incoming: list[tuple],
-                         timeout_s: float | None, stream, peer_layouts: dict | None = None) -> None:
+                         timeout_s: float | None, stream, peer_layouts: dict | None = None,
+                         wait_pulled: bool = True) -> None:
         """The transfers of ``exchange`` in world_size-1 rounds.
 
         A transfer a->b belongs to round (b - a) mod world_size on both of its
@@ -377,7 +494,7 @@ class TransferEndpoint:
             rounds.setdefault((self.rank - item[0]) % world, ([], []))[1].append(item)
         for j in sorted(rounds):
             out, inc = rounds[j]
-            self.exchange(mode, local, out, inc, timeout_s, stream, peer_layouts)
+            self.exchange(mode, local, out, inc, timeout_s, stream, peer_layouts, wait_pulled)
 
     def read_done(self, src_rank: int) -> int:
         out = ctypes.c_uint64(0)
@@ -426,6 +543,10 @@ class TransferEndpoint:
     def close(self) -> None:
         if self.closed:
             return
+        try:
+            self.poll_deferred(wait=True)
+        except Exception as exc:  # noqa: BLE001 - best effort at shutdown
+            logger.warning("reading deferred grants failed: %s", exc)
         for link in self.links.values():
             for key in link.closers:
                 try:

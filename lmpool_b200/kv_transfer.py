@@ -426,6 +426,22 @@ def transfer_mode() -> str:
     return mode
 
 
+def source_return() -> str:
+    """When ``swap_in`` returns on the source in pull mode, from
+    ``LMPOOL_B200_SOURCE_RETURN``: ``read`` (default) once the destination
+    reports its blocks were read, or ``granted`` once the grant is enqueued
+    on the source's stream. ``granted`` frees the source's worker for the
+    whole copy, as the reference's host-asynchronous NCCL send does
+    (kv_transfer.py:466-467); the release of the source blocks stays safe
+    because LMPool sends finalize only after the destination acknowledged its
+    execute (data_plane.py:369-412), i.e. after the read. The grant's
+    outcome is checked at the source's next transfer call."""
+    value = os.environ.get("LMPOOL_B200_SOURCE_RETURN", "read").strip().lower()
+    if value not in ("read", "granted"):
+        raise RuntimeError(f"LMPOOL_B200_SOURCE_RETURN must be 'read' or 'granted', got {value!r}")
+    return value
+
+
 def _endpoint(rank: int, world_size: int, device: int, max_blocks: int) -> TransferEndpoint:
     ep = _ENDPOINTS.get(device)
     if ep is not None and (ep.rank != rank or ep.world_size != world_size or ep.mailbox.max_blocks < max_blocks):
@@ -520,6 +536,13 @@ def prewarm_p2p_pairs(
         payload_maps[other.rank] = pl_layout.with_base(ptr)
         pair = tuple(sorted((rank, other.rank)))
         _P2P_GROUPS[pair] = link
+    # Every pair restarts from token 1 with zeroed mailbox words and CTA
+    # counters on both sides (no transfer is in flight during prewarm), so a
+    # pair disabled by an earlier timeout comes back without a shutdown.
+    ep.poll_deferred(wait=True)
+    for peer in list(ep.links):
+        ep.reset_pair(peer, torch.cuda.current_stream(device))
+    torch.cuda.synchronize(device)
     dist.barrier()
 
     observations = []
@@ -529,14 +552,14 @@ def prewarm_p2p_pairs(
         payload.fill_(float(src + 1) if rank == src else 0.0)
         # Warm-up transfer: first touch of the peer mapping and kernels.
         if rank == src:
-            _source_side(ep, dst, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[dst])
+            _source_side(ep, dst, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[dst], wait=True)
         elif rank == dst:
             _destination_side(ep, src, ids, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[src])
         dist.barrier()
         if rank == src:
             torch.cuda.synchronize(device)
             started = time.perf_counter()
-            _source_side(ep, dst, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[dst])
+            _source_side(ep, dst, ids, timeout_s, stream, local=pl_layout, remote=payload_maps[dst], wait=True)
             torch.cuda.synchronize(device)
             observations.append({
                 "src_gpu": src,
@@ -560,6 +583,7 @@ def prewarm_p2p_pairs(
 
 def _run_exchange(ep: TransferEndpoint, local: CacheLayout, outgoing: list, incoming: list,
                   timeout_s: float | None, stream, peer_layouts: dict | None, what: str) -> None:
+    ep.poll_deferred()
     ep.reset_status(stream)
     ep.exchange(ep.mode, local, outgoing, incoming, timeout_s, stream, peer_layouts)
     peers = [o[0] for o in outgoing] + [i[0] for i in incoming]
@@ -577,14 +601,24 @@ def _destination_side(ep: TransferEndpoint, src_rank: int, src_ids: List[int], d
 
 
 def _source_side(ep: TransferEndpoint, dst_rank: int, src_ids: List[int], timeout_s: float | None, stream,
-                 local: CacheLayout | None = None, remote: CacheLayout | None = None) -> None:
-    """Give ``src_ids`` to ``dst_rank`` (blocks until the destination holds them).
+                 local: CacheLayout | None = None, remote: CacheLayout | None = None,
+                 wait: bool | None = None) -> None:
+    """Give ``src_ids`` to ``dst_rank``: blocks until the destination holds
+    them, or, in pull mode with ``wait`` false (default from
+    :func:`source_return`), returns once the grant is enqueued on ``stream``.
     In pull mode the destination reads the ids it was given itself, so the
     source uploads none."""
+    what = f"transfer {ep.rank}->{dst_rank} (source, {ep.mode})"
+    if ep.mode == "pull":
+        if wait is None:
+            wait = source_return() == "read"
+        if not wait:
+            ep.grant_deferred(ep.get_link(dst_rank), len(src_ids), timeout_s, stream, what)
+            return
     sids = None if ep.mode == "pull" else _upload(ep.device, stream, _id_array(src_ids))[0]
     layouts = {dst_rank: remote} if remote is not None else None
     _run_exchange(ep, ep.cache if local is None else local, [(dst_rank, sids, len(src_ids))], [], timeout_s,
-                  stream, layouts, f"transfer {ep.rank}->{dst_rank} (source, {ep.mode})")
+                  stream, layouts, what)
 
 
 def _peer_cache(ep: TransferEndpoint, peer: int) -> CacheLayout:
@@ -795,6 +829,7 @@ def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, 
     out = [(d, dev_ids[i], n) for d, i, n in out_spec]
     inc = [(s_, dev_ids[i], dev_ids[j], n) for s_, i, j, n in in_spec]
     mode = ep.mode if mode is None else mode
+    ep.poll_deferred()
     ep.reset_status(stream)
     if schedule == "rotated":
         ep.exchange_rotated(mode, ep.cache, out, inc, timeout_s, stream)

@@ -71,14 +71,16 @@ def test_tuning_roundtrip_and_validation(kvx_lib):
     old = _capi.Tuning()
     assert kvx_lib.kvx_get_tuning(ctypes.byref(old)) == 0
     try:
-        t = _capi.Tuning(variant=2, ctas_per_sm=1, tile_bytes=32768, stages=8)
+        t = _capi.Tuning(variant=2, ctas_per_sm=1, tile_bytes=32768, stages=8, store_pdl=2)
         assert kvx_lib.kvx_set_tuning(ctypes.byref(t)) == 0
         back = _capi.Tuning()
         kvx_lib.kvx_get_tuning(ctypes.byref(back))
-        assert (back.variant, back.ctas_per_sm, back.tile_bytes, back.stages) == (2, 1, 32768, 8)
+        assert (back.variant, back.ctas_per_sm, back.tile_bytes, back.stages, back.store_pdl) == (2, 1, 32768, 8, 2)
         assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(variant=3))) == _capi.KVX_EINVAL
         assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(tile_bytes=100))) == _capi.KVX_EINVAL
         assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(stages=5))) == _capi.KVX_EINVAL
+        assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(store_pdl=3))) == _capi.KVX_EINVAL
+        assert kvx_lib.kvx_set_tuning(ctypes.byref(_capi.Tuning(reserved=1))) == _capi.KVX_EINVAL
     finally:
         kvx_lib.kvx_set_tuning(ctypes.byref(old))
 

@@ -530,6 +530,23 @@ def test_all_partner_swap_batch_matches_oracle(require_gpu, mode, schedule):
 
 # -- destination-driven (pull) mode ------------------------------------------------
 
+def _pull_steps(ep_dst, link_to_src, ep_src, link_to_dst, sids, dids, n, s_dst, s_src, timeout=5.0,
+                grant=True, wait_pulled=True):
+    """One pull transfer in dependency order: request (destination), grant
+    (source), wait for the grant + pull (destination), wait_pulled (source).
+    On one stream every wait is satisfied by a kernel that finished before
+    it; on two GPUs each wait is satisfied by a launch issued before it."""
+    token = ep_dst.next_token(ep_src.rank)
+    ep_dst.request(link_to_src, n, token, s_dst)
+    if grant:
+        ep_src.grant(link_to_dst, n, timeout, s_src)
+    ep_dst.wait_done(ep_src.rank, token, timeout if grant else 0.2, s_dst)
+    ep_dst.pull(ep_dst.cache, [(link_to_src, link_to_src.cache, sids, dids, n, token)], s_dst)
+    if wait_pulled:
+        ep_src.wait_pulled(ep_dst.rank, timeout, s_src)
+    return token
+
+
 @pytest.mark.parametrize("variant", [1, 2], ids=["register", "bulk"])
 def test_loopback_pull_on_one_stream(require_gpu, variant):
     """Rank 1 pulls rank 0's blocks (same GPU) and signals rank 0, which waits
@@ -548,9 +565,7 @@ def test_loopback_pull_on_one_stream(require_gpu, variant):
             dst_ids = kvgen.seeded_perm(24, 80 + round_)[:8]
             ep0.status.zero_()
             ep1.status.zero_()
-            token = ep1.next_token(0)
-            ep1.pull(ep1.cache, [(link10, link10.cache, _ids(src_ids, 0), _ids(dst_ids, 0), 8, token)], s)
-            ep0.wait_pulled(1, 5.0, s)
+            _pull_steps(ep1, link10, ep0, link01, _ids(src_ids, 0), _ids(dst_ids, 0), 8, s, s)
             ep1.check_status(s, "destination")
             ep0.check_status(s, "source")
             c_oracle.swap_planned(src_cpu, src_ids, dst_cpu, dst_ids, nthreads=4)
@@ -581,8 +596,15 @@ def test_one_pull_launch_reads_several_sources(require_gpu):
     src_ids = {r: kvgen.seeded_perm(N, 620 + r)[:counts[r]] for r in (0, 1, 2)}
     for e in eps:
         e.status.zero_()
+    tokens = {r: eps[3].next_token(r) for r in (0, 1, 2)}
+    for r in (0, 1, 2):
+        eps[3].request(to_src[r], counts[r], tokens[r], s)
+    for r in (0, 1, 2):
+        eps[r].grant(eps[r].get_link(3), counts[r], 5.0, s)
+    for r in (0, 1, 2):
+        eps[3].wait_done(r, tokens[r], 5.0, s)
     eps[3].pull(eps[3].cache, [(to_src[r], to_src[r].cache, _ids(src_ids[r], 0), _ids(dst_ids[r], 0), counts[r],
-                                eps[3].next_token(r)) for r in (0, 1, 2)], s)
+                                tokens[r]) for r in (0, 1, 2)], s)
     for r in (0, 1, 2):
         eps[r].wait_pulled(3, 5.0, s)
     for e in eps:
@@ -609,8 +631,7 @@ def test_wait_pulled_times_out_and_stale_pulls_do_not_count(require_gpu):
     ep0.status.zero_()
     ep1.status.zero_()
     ids = _ids([1, 2], 0)
-    ep1.pull(ep1.cache, [(link10, link10.cache, ids, ids, 2, ep1.next_token(0))], s)
-    ep0.wait_pulled(1, 2.0, s)                  # consumes that pull
+    _pull_steps(ep1, link10, ep0, link01, ids, ids, 2, s, s, timeout=2.0)   # consumes that pull
     ep0.check_status(s, "first")
     ep0.wait_pulled(1, 0.2, s)                  # the same pull cannot satisfy a second wait
     with pytest.raises(_capi.KvxError, match="timed out"):
@@ -634,8 +655,7 @@ def test_two_gpus_one_process_pull_over_nvlink(require_gpu, variant):
         dst_ids = kvgen.seeded_perm(64, 19)[:16]
         ep0.status.zero_()
         ep1.status.zero_()
-        ep1.pull(ep1.cache, [(link10, link10.cache, _ids(src_ids, 1), _ids(dst_ids, 1), 16, ep1.next_token(0))], s1)
-        ep0.wait_pulled(1, 10.0, s0)
+        _pull_steps(ep1, link10, ep0, link01, _ids(src_ids, 1), _ids(dst_ids, 1), 16, s1, s0, timeout=10.0)
         ep1.check_status(s1, "destination")
         ep0.check_status(s0, "source")
         c_oracle.swap_planned(src_cpu, src_ids, dst_cpu, dst_ids, nthreads=8)
@@ -644,3 +664,129 @@ def test_two_gpus_one_process_pull_over_nvlink(require_gpu, variant):
         ep1.close()
     finally:
         lib.kvx_set_tuning(ctypes.byref(old))
+
+
+def test_pull_without_a_grant_moves_nothing_and_reports_failure(require_gpu):
+    """A destination whose request is never granted waits (bounded), its
+    pull copies nothing, and the source learns of it as a failed pull."""
+    shape = (2, 3, 10, 16, 2, 32)
+    _, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 21)
+    s = torch.cuda.current_stream(0)
+    ep0.status.zero_()
+    ep1.status.zero_()
+    ids = _ids([1, 2, 3], 0)
+    _pull_steps(ep1, link10, ep0, link01, ids, ids, 3, s, s, grant=False)
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep1.check_status(s, "destination")
+    with pytest.raises(_capi.KvxError, match="reported failure"):
+        ep0.check_status(s, "source")
+    assert _same_bits(dst, dst_cpu)
+    ep0.close()
+    ep1.close()
+
+
+def test_push_arm_and_pull_request_never_satisfy_each_other(require_gpu):
+    """Two ends that disagree on the mode fail on both sides without moving data."""
+    shape = (2, 3, 10, 16, 2, 32)
+    _, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 22)
+    s = torch.cuda.current_stream(0)
+    ids = _ids([4, 5], 0)
+    # destination pulls, source pushes
+    ep0.status.zero_()
+    ep1.status.zero_()
+    token = ep1.next_token(0)
+    ep1.request(link10, 2, token, s)
+    ep0.wait_armed(link01, 2, 2.0, s)
+    ep0.push(ep0.cache, [(link01, link01.cache, ids, 2)], s)
+    ep1.wait_done(0, token, 2.0, s)
+    ep1.pull(ep1.cache, [(link10, link10.cache, ids, ids, 2, token)], s)
+    with pytest.raises(_capi.KvxError, match="different block count"):
+        ep0.check_status(s, "source")
+    with pytest.raises(_capi.KvxError, match="reported failure"):
+        ep1.check_status(s, "destination")
+    assert _same_bits(dst, dst_cpu)
+    # destination pushes (publishes ids), source grants a pull
+    ep0.status.zero_()
+    ep1.status.zero_()
+    token = ep1.next_token(0)
+    ep1.publish(link10, ids, 2, token, s)
+    ep0.grant(link01, 2, 2.0, s)
+    ep1.wait_done(0, token, 2.0, s)
+    with pytest.raises(_capi.KvxError, match="different block count"):
+        ep0.check_status(s, "source")
+    with pytest.raises(_capi.KvxError, match="reported failure"):
+        ep1.check_status(s, "destination")
+    assert _same_bits(dst, dst_cpu)
+    ep0.close()
+    ep1.close()
+
+
+def test_a_reset_pair_recovers_after_an_injected_failure(require_gpu):
+    """A timeout reported on the host disables the pair; resetting both ends
+    (what prewarm does) brings it back from token 1, with no new mailbox."""
+    shape = (2, 3, 12, 16, 2, 32)
+    src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 23)
+    s = torch.cuda.current_stream(0)
+    ids_a = kvgen.seeded_perm(12, 24)[:4]
+    for _ in range(3):
+        ep0.status.zero_()
+        ep1.status.zero_()
+        _pull_steps(ep1, link10, ep0, link01, _ids(ids_a, 0), _ids(ids_a, 0), 4, s, s)
+        ep1.check_status(s, "destination")
+        ep0.check_status(s, "source")
+    # inject: the destination's status word reports a bulk-pipeline timeout
+    ep1.status.fill_(_capi.DEV_PIPE_TIMEOUT)
+    with pytest.raises(_capi.KvxError):
+        ep1.check_status(s, "destination", peers=[0])
+    with pytest.raises(RuntimeError, match="disabled"):
+        ep1.get_link(0)
+    for ep, peer in ((ep0, 1), (ep1, 0)):
+        ep.reset_pair(peer, s)
+    ep0.status.zero_()
+    ep1.status.zero_()
+    ids_b = kvgen.seeded_perm(12, 25)[:5]
+    dst_b = kvgen.seeded_perm(12, 26)[:5]
+    token = _pull_steps(ep1, ep1.get_link(0), ep0, ep0.get_link(1), _ids(ids_b, 0), _ids(dst_b, 0), 5, s, s)
+    assert token == 1
+    ep1.check_status(s, "destination")
+    ep0.check_status(s, "source")
+    c_oracle.swap_planned(src_cpu, ids_a, dst_cpu, ids_a, nthreads=2)
+    c_oracle.swap_planned(src_cpu, ids_b, dst_cpu, dst_b, nthreads=2)
+    assert _same_bits(dst, dst_cpu)
+    ep0.close()
+    ep1.close()
+
+
+@pytest.mark.skipif(device_count() < 2, reason="needs 2 GPUs")
+def test_pull_reads_what_the_source_wrote_before_its_grant(require_gpu):
+    """Ordering: the source's stream writes its blocks (a long local move)
+    and only then grants; the destination, on another GPU, requests and pulls
+    at once. The pulled blocks are the newly written ones, bit for bit."""
+    shape = (2, 36, 96, 64, 8, 128)
+    src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 1, shape, 27)
+    s0, s1 = torch.cuda.current_stream(0), torch.cuda.current_stream(1)
+    staging = kvgen.seeded_perm(96, 28)[:32]
+    blocks = kvgen.seeded_perm(96, 29)
+    blocks = [b for b in blocks if b not in set(staging)][:32]
+    targets = kvgen.seeded_perm(96, 30)[:32]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    from lmpool_b200 import kv_transfer as kt
+    ep0.status.zero_()
+    ep1.status.zero_()
+    token = ep1.next_token(0)
+    ep1.request(link10, 32, token, s1)
+    kt._launch_move(0, ep0.cache, ep0.cache, _ids(staging, 0), _ids(blocks, 0), 32, status, s0)
+    ep0.grant(link01, 32, 10.0, s0)
+    ep1.wait_done(0, token, 10.0, s1)
+    ep1.pull(ep1.cache, [(link10, link10.cache, _ids(blocks, 1), _ids(targets, 1), 32, token)], s1)
+    ep0.wait_pulled(1, 10.0, s0)
+    ep1.check_status(s1, "destination")
+    ep0.check_status(s0, "source")
+    assert int(status.item()) == 0
+    moved = src_cpu.clone()
+    moved[:, :, blocks] = src_cpu[:, :, staging]
+    c_oracle.swap_planned(moved, blocks, dst_cpu, targets, nthreads=8)
+    assert _same_bits(dst, dst_cpu)
+    assert _same_bits(src, moved)
+    ep0.close()
+    ep1.close()

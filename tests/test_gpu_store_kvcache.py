@@ -99,6 +99,70 @@ def test_out_of_range_slots_are_flagged_and_skipped(require_gpu):
     assert kc.view(N * bs, -1)[0].eq(1).all() and kc.view(N * bs, -1)[1:].abs().sum() == 0
 
 
+@pytest.fixture(params=[1, 2], ids=["pdl", "no_pdl"])
+def store_launch(request, require_gpu):
+    """Run the test with store_kvcache launched with programmatic dependent
+    launch (the default) and without it."""
+    import ctypes
+
+    lib = require_gpu
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(ctypes.byref(old))
+    t = _capi.Tuning()
+    ctypes.memmove(ctypes.byref(t), ctypes.byref(old), ctypes.sizeof(t))
+    t.store_pdl = request.param
+    assert lib.kvx_set_tuning(ctypes.byref(t)) == 0
+    yield request.param
+    lib.kvx_set_tuning(ctypes.byref(old))
+
+
+def test_store_sees_rows_the_kernel_before_it_wrote(store_launch):
+    """Each step writes new K/V rows with a kernel and stores them at once,
+    eagerly and captured in a graph (as a model layer does): the store reads
+    the new rows every time, with or without programmatic dependent launch."""
+    T, H, D, bs, N, L = 64, 8, 128, 16, 96, 6
+    kc = torch.zeros(L, N, bs, H, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    key = torch.zeros(L, T, H, D, dtype=torch.bfloat16, device=DEV)
+    value = torch.zeros_like(key)
+    src_k = kvgen.seeded_cache((L, T, H, D), 130).to(DEV)
+    src_v = kvgen.seeded_cache((L, T, H, D), 131).to(DEV)
+    slots = kvgen.slot_mapping(T, N * bs, 132, skip_fraction=0.1).to(DEV)
+    scale = torch.ones((), dtype=torch.bfloat16, device=DEV)
+
+    def step():
+        for layer in range(L):
+            torch.mul(src_k[layer], scale, out=key[layer])        # a kernel writes the rows ...
+            torch.mul(src_v[layer], scale, out=value[layer])
+            store_kvcache(key[layer], value[layer], kc[layer], vc[layer], slots, bs)   # ... stored right after
+
+    def expected():
+        kc_c = torch.zeros(L, N, bs, H, D, dtype=torch.bfloat16)
+        vc_c = torch.zeros_like(kc_c)
+        for layer in range(L):
+            c_oracle.store_kvcache((src_k[layer] * scale).cpu(), (src_v[layer] * scale).cpu(), kc_c[layer],
+                                   vc_c[layer], slots.cpu(), bs)
+        return kc_c, vc_c
+
+    for rnd in range(5):
+        scale.fill_(float(rnd + 1))
+        step()
+    torch.cuda.synchronize()
+    kt.check_device_status(0)
+    kc_c, vc_c = expected()
+    assert _same_bits(kc, kc_c) and _same_bits(vc, vc_c)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for rnd in range(5):
+        scale.fill_(float(rnd + 7))
+        graph.replay()
+        torch.cuda.synchronize()
+        kc_c, vc_c = expected()
+        assert _same_bits(kc, kc_c) and _same_bits(vc, vc_c)
+    kt.check_device_status(0)
+
+
 def test_captured_in_a_cuda_graph(require_gpu):
     """The decode path captures store_kvcache (model_runner.py:630-683): no sync, no allocation."""
     T, H, D, bs, N = 32, 8, 128, 16, 64

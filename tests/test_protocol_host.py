@@ -28,6 +28,8 @@ def _endpoint(rank: int, world: int):
     ep.pull = lambda local, sources, stream: calls.append(
         ("pull", [(link.peer, layout, n, token) for link, layout, _s, _d, n, token in sources]))
     ep.wait_pulled = lambda dst, t, stream: calls.append(("wait_pulled", dst))
+    ep.request = lambda link, n, token, stream: calls.append(("request", link.peer, n, token))
+    ep.grant = lambda link, n, t, stream, status_ptr=None: calls.append(("grant", link.peer, n))
     return ep, calls
 
 
@@ -41,13 +43,23 @@ def test_push_arms_everything_before_any_wait():
     assert calls[5] == ("wait_done", 1, 1) and calls[6] == ("wait_done", 3, 1)
 
 
-def test_pull_reads_everything_before_any_wait():
+def test_pull_requests_and_grants_everything_before_any_wait():
     ep, calls = _endpoint(2, 4)
     ep.exchange("pull", "local", [(0, "i0", 5)], [(1, "s1", "d1", 3), (3, "s3", "d3", 0)], 1.0, None,
                 peer_layouts={3: "payload3"})
-    assert [c[0] for c in calls] == ["pull", "wait_pulled"]
-    assert calls[0] == ("pull", [(1, "cache1", 3, 1), (3, "payload3", 0, 1)])
-    assert calls[1] == ("wait_pulled", 0)
+    assert [c[0] for c in calls] == ["request", "request", "grant", "wait_done", "wait_done", "pull",
+                                     "wait_pulled"]
+    assert calls[0] == ("request", 1, 3, 1) and calls[1] == ("request", 3, 0, 1)
+    assert calls[2] == ("grant", 0, 5)
+    assert calls[3] == ("wait_done", 1, 1) and calls[4] == ("wait_done", 3, 1)
+    assert calls[5] == ("pull", [(1, "cache1", 3, 1), (3, "payload3", 0, 1)])
+    assert calls[6] == ("wait_pulled", 0)
+
+
+def test_a_source_that_returns_once_granted_skips_the_read_wait():
+    ep, calls = _endpoint(1, 2)
+    ep.exchange("pull", "local", [(0, "i0", 2)], [], 1.0, None, wait_pulled=False)
+    assert calls == [("grant", 0, 2)]
 
 
 def test_tokens_grow_per_source_across_exchanges():
@@ -112,9 +124,10 @@ def test_rotated_schedule_puts_each_transfer_in_round_peer_offset():
 def _simulate(streams: dict[int, list], mode: str) -> None:
     """Run every rank's recorded device steps against one another, in any
     interleaving, with the mailbox semantics of the kernels: an arm slot per
-    (source, destination) that must be free when published, a done token the
-    destination waits for, a pulled report the source waits for. Raises on a
-    deadlock (no rank can make progress) or a clobbered mailbox."""
+    (source, destination) that must be free when published or requested, a
+    done token (push completion or pull grant) the destination waits for, a
+    pulled report the source waits for. Raises on a deadlock (no rank can
+    make progress) or a clobbered mailbox."""
     arm, done, pulled = {}, {}, {}
     pos = {r: 0 for r in streams}
     while any(pos[r] < len(streams[r]) for r in streams):
@@ -123,12 +136,16 @@ def _simulate(streams: dict[int, list], mode: str) -> None:
             while pos[r] < len(steps):
                 step = steps[pos[r]]
                 kind = step[0]
-                if kind == "publish":                 # r is the destination, step[1] the source
+                if kind in ("publish", "request"):    # r is the destination, step[1] the source
                     assert (step[1], r) not in arm, "arm published twice before the source used it"
                     arm[(step[1], r)] = step[3]
                 elif kind == "wait_armed":
                     if (r, step[1]) not in arm:
                         break
+                elif kind == "grant":                 # r is the source, step[1] the destination
+                    if (r, step[1]) not in arm:
+                        break
+                    done[(r, step[1])] = arm.pop((r, step[1]))
                 elif kind == "push":
                     for peer, _layout, _n in step[1]:
                         done[(r, peer)] = arm.pop((r, peer))
@@ -174,17 +191,36 @@ def test_every_rank_finishes_for_random_transfer_sets(mode, schedule, world, see
     _simulate(streams, mode)
 
 
-def test_simulator_detects_a_deadlock():
-    """Two sequential one-way calls in opposite directions, push mode: each
-    rank first waits for the other's arm."""
+@pytest.mark.parametrize("mode", ["push", "pull"])
+def test_simulator_detects_a_deadlock(mode):
+    """Two sequential one-way calls in opposite directions: each rank first
+    waits for the other's arm (push) or request (pull)."""
     a, ca = _endpoint(0, 2)
     b, cb = _endpoint(1, 2)
-    a.exchange("push", "local", [(1, "i", 1)], [], 1.0, None)
-    a.exchange("push", "local", [], [(1, "s", "d", 1)], 1.0, None)
-    b.exchange("push", "local", [(0, "i", 1)], [], 1.0, None)
-    b.exchange("push", "local", [], [(0, "s", "d", 1)], 1.0, None)
+    a.exchange(mode, "local", [(1, "i", 1)], [], 1.0, None)
+    a.exchange(mode, "local", [], [(1, "s", "d", 1)], 1.0, None)
+    b.exchange(mode, "local", [(0, "i", 1)], [], 1.0, None)
+    b.exchange(mode, "local", [], [(0, "s", "d", 1)], 1.0, None)
     with pytest.raises(AssertionError, match="deadlock"):
-        _simulate({0: ca, 1: cb}, "push")
+        _simulate({0: ca, 1: cb}, mode)
+
+
+def test_sequential_calls_in_one_direction_at_a_time_finish_in_pull_mode():
+    """What LMPool issues (one plan per pair at a time): 0->1, then 1->0,
+    both ranks calling in the same order, with the source returning once its
+    grant is enqueued or after the read."""
+    for wait in (True, False):
+        a, ca = _endpoint(0, 2)
+        b, cb = _endpoint(1, 2)
+        a.exchange("pull", "local", [(1, "i", 2)], [], 1.0, None, wait_pulled=wait)
+        b.exchange("pull", "local", [], [(0, "s", "d", 2)], 1.0, None)
+        b.exchange("pull", "local", [(0, "i", 3)], [], 1.0, None, wait_pulled=wait)
+        a.exchange("pull", "local", [], [(1, "s", "d", 3)], 1.0, None)
+        streams = {0: ca, 1: cb}
+        if not wait:   # the reads nobody waits for leave their reports behind
+            streams[0] = ca + [("wait_pulled", 1)]
+            streams[1] = cb + [("wait_pulled", 0)]
+        _simulate(streams, "pull")
 
 
 def _batch_setup(monkeypatch):
@@ -251,6 +287,8 @@ def test_every_enqueued_step_marks_the_status_word_unchecked():
     link = PeerLink(peer=1, mailbox=_capi.Mailbox(), cache=lay)
     ids = torch.zeros(2, dtype=torch.int64)
     steps = [
+        lambda: ep.request(link, 2, 1, None),
+        lambda: ep.grant(link, 2, 1.0, None),
         lambda: ep.publish(link, ids, 2, 1, None),
         lambda: ep.wait_done(1, 1, 1.0, None),
         lambda: ep.wait_armed(link, 2, 1.0, None),
