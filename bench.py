@@ -1479,6 +1479,8 @@ def main() -> None:
     ap.add_argument("--pull", action="store_true", help="pair1p: destination pulls instead of source pushing")
     ap.add_argument("--pair-mode", choices=["auto", "push", "pull"], default="auto",
                     help="N>1 exchanges that send both ways at once (phase A, config 5): auto = push")
+    ap.add_argument("--store-pdl", choices=["auto", "on", "off"], default="auto",
+                    help="store_kvcache launch with programmatic dependent launch (auto = on)")
     ap.add_argument("--quick", action="store_true",
                     help="1 GPU: time the headline loop only (no sweep, e2e or CPU baseline); for profiling")
     args = ap.parse_args()
@@ -1493,8 +1495,9 @@ def main() -> None:
 
     from lmpool_b200 import _capi
 
-    if args.variant != "auto":
-        t = _capi.Tuning(variant={"register": 1, "bulk": 2}[args.variant])
+    if args.variant != "auto" or args.store_pdl != "auto":
+        t = _capi.Tuning(variant={"auto": 0, "register": 1, "bulk": 2}[args.variant],
+                         store_pdl={"auto": 0, "on": 1, "off": 2}[args.store_pdl])
         _capi.check(_capi.lib().kvx_set_tuning(_capi.ctypes.byref(t)), "kvx_set_tuning")
     if args.workload == "config5":
         res = bench_config5(args)

@@ -2,9 +2,9 @@
 
 Counterpart of LMPool's ``benchmarks/benchmark_kv_transfer.py``: the same
 command-line flags, the same two-process pair case (rank 0's blocks
-``0..B-1`` move to rank 1's blocks ``B..2B-1``, filled with per-block
-constants and checked afterwards, benchmark_kv_transfer.py:75-89, :92-193),
-and the same result schema (``{"metadata": ..., "results": [...]}`` with
+``0..B-1`` move to rank 1's blocks ``B..2B-1``, benchmark_kv_transfer.py:92-193;
+here seeded random caches checked afterwards by per-block digests of the
+raw bytes on both ranks), and the same result schema (``{"metadata": ..., "results": [...]}`` with
 ``num_transfer_blocks``, ``bytes_per_iteration``, mean/p50/p95 latency and
 GiB/s per row, :176-193, :334-350). LMPool's own profile builder
 (benchmarks/build_transfer_profile.py -> transfer_profile.py:113-196) reads
@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import platform
 import queue
@@ -36,11 +37,19 @@ _DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torc
 
 
 def parse_block_counts(raw: str, fallback: int) -> list[int]:
-    """benchmark_kv_transfer.py:196-201: a stable, deduplicated sweep."""
-    values = [fallback] if not raw.strip() else [int(item) for item in raw.split(",")]
-    if any(value < 1 for value in values):
-        raise ValueError("transfer block counts must all be >= 1")
-    return list(dict.fromkeys(values))
+    """Block counts of the sweep in first-seen order, each once; ``fallback``
+    when the list is empty. Same contract as the reference's flag
+    (benchmark_kv_transfer.py:196-201): every count must be positive."""
+    sweep: list[int] = []
+    for piece in (raw or "").split(","):
+        if not piece.strip():
+            continue
+        count = int(piece)
+        if count < 1:
+            raise ValueError(f"transfer block counts must all be >= 1, got {count}")
+        if count not in sweep:
+            sweep.append(count)
+    return sweep or [int(fallback)]
 
 
 def parse_args(argv=None):
@@ -62,23 +71,22 @@ def parse_args(argv=None):
     return args
 
 
-def _fill_source_blocks(kv_cache: torch.Tensor, blocks: list[int]) -> None:
-    for block_id in blocks:
-        kv_cache[0, :, block_id].fill_(float(block_id + 1))
-        kv_cache[1, :, block_id].fill_(float(block_id + 1001))
+def _block_digests(kv_cache: torch.Tensor, blocks: list[int]) -> list[int]:
+    """One 64-bit digest per listed block over its raw bytes (every layer,
+    both planes): a wrapping dot product of the block's 32-bit words with
+    fixed odd weights. Source and destination compare digests, so the check
+    sees the actual bytes, including two blocks swapped or a layer moved."""
+    idx = torch.tensor(blocks, dtype=torch.long, device=kv_cache.device)
+    words = kv_cache.index_select(2, idx).transpose(0, 2).reshape(len(blocks), -1).view(torch.int32).to(torch.int64)
+    gen = torch.Generator().manual_seed(1234)
+    weights = (torch.randint(0, 2**31 - 1, (words.shape[1],), generator=gen, dtype=torch.int64) * 2 + 1)
+    return (words * weights.to(words.device)).sum(dim=1).tolist()
 
 
-def _check_target_blocks(kv_cache: torch.Tensor, src_blocks: list[int], dst_blocks: list[int]) -> bool:
-    for src_block, dst_block in zip(src_blocks, dst_blocks):
-        if not torch.all(kv_cache[0, :, dst_block] == float(src_block + 1)).item():
-            return False
-        if not torch.all(kv_cache[1, :, dst_block] == float(src_block + 1001)).item():
-            return False
-    return True
-
-
-def _percentile95(values: list[float]) -> float:
-    return max(values) if len(values) < 2 else statistics.quantiles(values, n=20)[18]
+def _p95(values: list[float]) -> float:
+    """Nearest-rank 95th percentile."""
+    ordered = sorted(values)
+    return ordered[max(0, math.ceil(0.95 * len(ordered)) - 1)]
 
 
 def _worker(rank: int, args, blocks: int, port: int, out) -> None:
@@ -94,10 +102,9 @@ def _worker(rank: int, args, blocks: int, port: int, out) -> None:
         dtype = _DTYPES[args.resolved_dtype]
         src_blocks = list(range(blocks))
         dst_blocks = list(range(blocks, 2 * blocks))
-        cache = torch.zeros(2, args.num_layers, 2 * blocks, args.block_size, args.num_kv_heads, args.head_dim,
+        cache = torch.empty(2, args.num_layers, 2 * blocks, args.block_size, args.num_kv_heads, args.head_dim,
                             dtype=dtype, device=f"cuda:{rank}")
-        if rank == 0:
-            _fill_source_blocks(cache, src_blocks)
+        cache.normal_(generator=torch.Generator(device=f"cuda:{rank}").manual_seed(100 + rank))
         kt.register_kv_cache(cache, args.num_layers)
         kt.prewarm_p2p_pairs([(0, 1)], num_layers=args.num_layers, block_size=args.block_size,
                              num_kv_heads=args.num_kv_heads, head_dim=args.head_dim, num_blocks=blocks, dtype=dtype)
@@ -120,13 +127,15 @@ def _worker(rank: int, args, blocks: int, port: int, out) -> None:
             if iteration >= args.warmup:
                 host_ms.append(elapsed)
                 dev_ms.append(e0.elapsed_time(e1))
-        ok = _check_target_blocks(cache, src_blocks, dst_blocks) if rank == 1 else True
+        digests = [None, None]
+        dist.all_gather_object(digests, _block_digests(cache, src_blocks if rank == 0 else dst_blocks))
+        ok = digests[0] == digests[1]
         bytes_per_iter = blocks * args.num_layers * args.block_size * args.num_kv_heads * args.head_dim * 2 \
             * cache.element_size()
         kt.shutdown()
         out.put({"rank": rank, "ok": bool(ok), "mean_ms": statistics.mean(host_ms),
-                 "p50_ms": statistics.median(host_ms), "p95_ms": _percentile95(host_ms),
-                 "device_mean_ms": statistics.mean(dev_ms), "device_p95_ms": _percentile95(dev_ms),
+                 "p50_ms": statistics.median(host_ms), "p95_ms": _p95(host_ms),
+                 "device_mean_ms": statistics.mean(dev_ms), "device_p95_ms": _p95(dev_ms),
                  "bytes_per_iter": bytes_per_iter})
         dist.destroy_process_group()
     except Exception as exc:  # noqa: BLE001 - reported to the parent
