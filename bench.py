@@ -284,7 +284,7 @@ def cpu_reference_c_port(g: dict, blocks: int, steps: int, warmup: int, min_seco
     from oracle import c_oracle
 
     threads = c_oracle.default_threads()
-    n = 2 * blocks + 64
+    n = 2 * blocks + 8
     shape = (2, g["L"], n, g["bs"], g["H"], g["D"])
     cache = torch.zeros(shape, dtype=torch.bfloat16)
     perm = seeded_perm(n, 0)

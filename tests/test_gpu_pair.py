@@ -790,3 +790,33 @@ def test_pull_reads_what_the_source_wrote_before_its_grant(require_gpu):
     assert _same_bits(src, moved)
     ep0.close()
     ep1.close()
+
+
+def test_a_deferred_grant_is_read_later_and_a_failed_one_disables_the_pair(require_gpu):
+    """The source can return once its grant is enqueued: the grant's outcome
+    is read from pinned memory after its event completes. A grant nobody
+    requested runs out (bounded) and disables the pair without raising in
+    an unrelated call."""
+    shape = (2, 3, 12, 16, 2, 32)
+    src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 31)
+    s = torch.cuda.current_stream(0)
+    ids, targets = kvgen.seeded_perm(12, 32)[:4], kvgen.seeded_perm(12, 33)[:4]
+    ep1.status.zero_()
+    token = ep1.next_token(0)
+    ep1.request(link10, 4, token, s)
+    ep0.grant_deferred(link01, 4, 5.0, s, "deferred grant")
+    ep1.wait_done(0, token, 5.0, s)
+    ep1.pull(ep1.cache, [(link10, link10.cache, _ids(ids, 0), _ids(targets, 0), 4, token)], s)
+    ep1.check_status(s, "destination")
+    ep0.poll_deferred(wait=True)
+    assert link01.poisoned is None and len(ep0._async_free) == ep0.ASYNC_SLOTS
+    c_oracle.swap_planned(src_cpu, ids, dst_cpu, targets, nthreads=2)
+    assert _same_bits(dst, dst_cpu)
+    # a grant with no request: its bounded wait runs out on the device
+    ep0.grant_deferred(link01, 4, 0.2, s, "unrequested grant")
+    ep0.poll_deferred(wait=True)
+    assert link01.poisoned and "timed out" in link01.poisoned
+    with pytest.raises(RuntimeError, match="disabled"):
+        ep0.get_link(1)
+    ep0.close()
+    ep1.close()
