@@ -300,3 +300,32 @@ def test_every_enqueued_step_marks_the_status_word_unchecked():
         ep.status_clean = True
         step()
         assert ep.status_clean is False
+
+
+def test_source_return_setting_picks_the_source_side_path(monkeypatch):
+    """Pull mode: 'read' runs the whole exchange (grant + wait for the read);
+    'granted' only enqueues a deferred grant. Push mode ignores the setting."""
+    from lmpool_b200 import kv_transfer as kt
+
+    ep, calls = _endpoint(0, 2)
+    ep.mode, ep.cache = "pull", "local"
+    ep.grant_deferred = lambda link, n, t, stream, what: calls.append(("grant_deferred", link.peer, n))
+    ran = []
+    monkeypatch.setattr(kt, "_run_exchange", lambda *a, **k: ran.append(a[2]))
+    monkeypatch.setattr(kt, "_upload", lambda device, stream, *arrays: [list(x) for x in arrays])
+    monkeypatch.setenv("LMPOOL_B200_SOURCE_RETURN", "granted")
+    kt._source_side(ep, 1, [3, 4, 5], 1.0, None)
+    assert calls == [("grant_deferred", 1, 3)] and ran == []
+    monkeypatch.setenv("LMPOOL_B200_SOURCE_RETURN", "read")
+    kt._source_side(ep, 1, [3, 4, 5], 1.0, None)
+    assert ran == [[(1, None, 3)]]
+    kt._source_side(ep, 1, [3, 4], 1.0, None, wait=False)     # an explicit wait overrides the setting
+    assert calls[-1] == ("grant_deferred", 1, 2)
+    ep.mode = "push"
+    monkeypatch.setenv("LMPOOL_B200_SOURCE_RETURN", "granted")
+    kt._source_side(ep, 1, [7], 1.0, None)
+    assert ran[-1] == [(1, [7], 1)]
+    monkeypatch.setenv("LMPOOL_B200_SOURCE_RETURN", "later")
+    ep.mode = "pull"
+    with pytest.raises(RuntimeError, match="LMPOOL_B200_SOURCE_RETURN"):
+        kt._source_side(ep, 1, [7], 1.0, None)
