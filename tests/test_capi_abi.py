@@ -99,6 +99,21 @@ def test_launch_entry_points_validate_before_touching_a_gpu(kvx_lib):
         _capi.KVX_EINVAL
     mb = _capi.Mailbox()
     assert kvx_lib.kvx_pair_publish(0, ctypes.byref(mb), 0, None, 0, 1, None) == _capi.KVX_EINVAL
+    good = _capi.Mailbox(base=1 << 20, max_peers=2, reserved=0, max_blocks=8)
+    # pull request: token 0 and tokens with the FAIL bit are refused, counts are bounded by the mailbox
+    assert kvx_lib.kvx_pair_request(0, ctypes.byref(good), 0, 4, 0, None) == _capi.KVX_EINVAL
+    assert kvx_lib.kvx_pair_request(0, ctypes.byref(good), 0, 4, 1 << 63, None) == _capi.KVX_EINVAL
+    assert kvx_lib.kvx_pair_request(0, ctypes.byref(good), 0, 9, 1, None) == _capi.KVX_EINVAL
+    assert kvx_lib.kvx_pair_request(0, ctypes.byref(good), 2, 4, 1, None) == _capi.KVX_EINVAL
+    # grant: a status word is required, ranks must fit both mailboxes
+    assert kvx_lib.kvx_pair_grant(0, ctypes.byref(good), ctypes.byref(good), 0, 1, 4, 10, None, None) == \
+        _capi.KVX_EINVAL
+    assert kvx_lib.kvx_pair_grant(0, ctypes.byref(good), ctypes.byref(good), 0, 5, 4, 10, 8, None) == \
+        _capi.KVX_EINVAL
+    assert kvx_lib.kvx_pair_grant(0, ctypes.byref(good), ctypes.byref(good), 0, 1, -1, 10, 8, None) == \
+        _capi.KVX_EINVAL
+    assert kvx_lib.kvx_mailbox_reset_peer(0, ctypes.byref(good), 2, None) == _capi.KVX_EINVAL
+    assert kvx_lib.kvx_mailbox_reset_peer(0, ctypes.byref(mb), 0, None) == _capi.KVX_EINVAL
     assert kvx_lib.kvx_store_kvcache(0, None, None, 0, 0, None, None, 0, 0, None, 1, 0, 16, 16, None, None) == \
         _capi.KVX_EINVAL
 
