@@ -1412,6 +1412,139 @@ def bench_pair_one_process(args) -> dict:
             "GB/s": P / (ms * 1e-3) / 1e9, "frac_nvlink": P / (ms * 1e-3) / 1e9 / NVLINK_NOMINAL_GBS, "verified": ok}
 
 
+def bench_pair_tuning(args) -> dict:
+    """``--workload pairtune``: the pair transfer at Qwen3-8B geometry on
+    cuda:0 and cuda:1 in one process, over a grid of launch settings (bulk
+    ring stages x tile x CTAs per SM, and the register engine), for push and
+    pull one way and both ways at once; plus plain peer copies (copy engine,
+    cudaMemcpyAsync on a chosen device's stream) over the same link. Every
+    wait is satisfied by a launch issued before it (one process, dependency
+    order). Measurement sweep behind the kernel's automatic choice."""
+    import itertools
+
+    from cuda.bindings import runtime as rt
+
+    from lmpool_b200 import _capi
+    from lmpool_b200.endpoint import TransferEndpoint
+    from lmpool_b200.layout import affine_layout
+
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("pairtune needs 2 GPUs")
+    g = dict(PAIRS)
+    B = args.blocks or 64
+    N = max(320, 4 * B + 8)
+    caches, eps = [], []
+    for d in (0, 1):
+        t = torch.empty((2, g["L"], N, g["bs"], g["H"], g["D"]), dtype=torch.bfloat16, device=f"cuda:{d}")
+        t.normal_(generator=torch.Generator(device=f"cuda:{d}").manual_seed(d))
+        caches.append(t)
+        ep = TransferEndpoint(d, 2, d, N)
+        ep.set_cache(affine_layout(t, g["L"]), t)
+        eps.append(ep)
+    links = {(0, 1): eps[0].link(eps[1].export_record()), (1, 0): eps[1].link(eps[0].export_record())}
+    perm = seeded_perm(N, 3)
+    src = {0: torch.tensor(perm[:B], device="cuda:0"), 1: torch.tensor(perm[B:2 * B], device="cuda:1")}
+    dst = {1: torch.tensor(perm[2 * B:3 * B], device="cuda:1"), 0: torch.tensor(perm[3 * B:4 * B], device="cuda:0")}
+    src_on = {1: src[0].to("cuda:1"), 0: src[1].to("cuda:0")}      # the source ids where the puller holds them
+    s = {0: torch.cuda.Stream(0), 1: torch.cuda.Stream(1)}
+    P = payload_bytes(g, B)
+
+    def push(pairs):
+        tokens = {(a, b): eps[b].next_token(a) for a, b in pairs}
+        for a, b in pairs:
+            eps[b].publish(links[(b, a)], dst[b], B, tokens[(a, b)], s[b])
+        for a, b in pairs:
+            eps[a].wait_armed(links[(a, b)], B, 30.0, s[a])
+        for a, b in pairs:
+            eps[a].push(eps[a].cache, [(links[(a, b)], links[(a, b)].cache, src[a], B)], s[a])
+        for a, b in pairs:
+            eps[b].wait_done(a, tokens[(a, b)], 30.0, s[b])
+
+    def pull(pairs):
+        tokens = {(a, b): eps[b].next_token(a) for a, b in pairs}
+        for a, b in pairs:
+            eps[b].request(links[(b, a)], B, tokens[(a, b)], s[b])
+        for a, b in pairs:
+            eps[a].grant(links[(a, b)], B, 30.0, s[a])
+        for a, b in pairs:
+            eps[b].wait_done(a, tokens[(a, b)], 30.0, s[b])
+            eps[b].pull(eps[b].cache, [(links[(b, a)], links[(b, a)].cache, src_on[b], dst[b], B, tokens[(a, b)])],
+                        s[b])
+        for a, b in pairs:
+            eps[a].wait_pulled(b, 30.0, s[a])
+
+    def timed(fn, reps=10) -> float:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(0)
+        torch.cuda.synchronize(1)
+        ev = {d: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for d in (0, 1)}
+        for d in (0, 1):
+            with torch.cuda.device(d):
+                ev[d][0].record(s[d])
+        for _ in range(reps):
+            fn()
+        for d in (0, 1):
+            with torch.cuda.device(d):
+                ev[d][1].record(s[d])
+        torch.cuda.synchronize(0)
+        torch.cuda.synchronize(1)
+        return max(ev[d][0].elapsed_time(ev[d][1]) for d in (0, 1)) / reps
+
+    lib = _capi.lib()
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(_capi.ctypes.byref(old))
+    grid = [(0, 0, 0, 0)]
+    for stages, tile, cps in itertools.product([4, 6, 8, 12], [8192, 16384, 32768, 65536], [0, 1, 2, 4]):
+        if 1024 + stages * tile <= 227 * 1024:
+            grid.append((2, cps, tile, stages))
+    grid += [(1, cps, tile, 0) for cps in (2, 4, 8) for tile in (16384, 32768, 65536)]
+    rows = []
+    try:
+        for variant, cps, tile, stages in grid:
+            _capi.check(lib.kvx_set_tuning(_capi.ctypes.byref(_capi.Tuning(variant, cps, tile, stages))),
+                        "kvx_set_tuning")
+            row = {"variant": {0: "auto", 1: "register", 2: "bulk"}[variant], "ctas_per_sm": cps, "tile": tile,
+                   "stages": stages}
+            for name, fn in (("push", lambda: push([(0, 1)])), ("pull", lambda: pull([(0, 1)])),
+                             ("push_both", lambda: push([(0, 1), (1, 0)])),
+                             ("pull_both", lambda: pull([(0, 1), (1, 0)]))):
+                row[name] = P / (timed(fn) * 1e-3) / 1e9
+            for d in (0, 1):
+                eps[d].check_status(s[d], "pairtune")
+            rows.append(row)
+    finally:
+        lib.kvx_set_tuning(_capi.ctypes.byref(old))
+    ok = torch.equal(caches[1][:, :, perm[2 * B:3 * B]].cpu().view(torch.int16),
+                     caches[0][:, :, perm[:B]].cpu().view(torch.int16)) and \
+        torch.equal(caches[0][:, :, perm[3 * B:4 * B]].cpu().view(torch.int16),
+                    caches[1][:, :, perm[B:2 * B]].cpu().view(torch.int16))
+    nbytes = 2 << 30
+    bufs = {d: (torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{d}"),
+                torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{d}")) for d in (0, 1)}
+
+    def cp(dst_t, src_t, dev):
+        err, = rt.cudaMemcpyAsync(dst_t.data_ptr(), src_t.data_ptr(), nbytes,
+                                  rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice, s[dev].cuda_stream)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaMemcpyAsync: {err}")
+
+    copies = {
+        "read_by_1_GB/s": nbytes / (timed(lambda: cp(bufs[1][0], bufs[0][0], 1), 5) * 1e-3) / 1e9,
+        "write_by_0_GB/s": nbytes / (timed(lambda: cp(bufs[1][0], bufs[0][0], 0), 5) * 1e-3) / 1e9,
+        "both_ways_read_GB/s_per_direction": nbytes / (timed(
+            lambda: (cp(bufs[1][0], bufs[0][0], 1), cp(bufs[0][1], bufs[1][1], 0)), 5) * 1e-3) / 1e9,
+    }
+    for ep in eps:
+        ep.close_links()
+    for ep in eps:
+        ep.close()
+    best = {k: max(rows, key=lambda r: r[k]) for k in ("push", "pull", "push_both", "pull_both")}
+    return {"workload": f"pair tuning sweep, cuda:0 <-> cuda:1, one process, Qwen3-8B geometry, B={B}",
+            "blocks": B, "cache_blocks": N, "unit": "GB/s per direction", "verified": bool(ok),
+            "automatic": rows[0], "best": best, "peer_copy": copies, "rows": rows}
+
+
 def bench_config5(args) -> dict | None:
     """``--workload config5``: config 5 alone on N GPUs (pairs)."""
     import torch.distributed as dist
@@ -1473,9 +1606,11 @@ def main() -> None:
     ap.add_argument("--cache-blocks", type=int, default=0,
                     help="1-GPU cache size in blocks (default: config 2's 2048); for small profiling cases")
     ap.add_argument("--blocks", type=int, default=0, help="1-GPU blocks moved per step (default 512)")
-    ap.add_argument("--workload", choices=["default", "config5", "pair1p", "store"], default="default",
+    ap.add_argument("--workload", choices=["default", "config5", "pair1p", "pairtune", "store"], default="default",
                     help="config5: benchmark config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
-                         "pair1p: one process, two GPUs, pair push (profiling); store: store_kvcache only")
+                         "pair1p: one process, two GPUs, pair push (profiling); pairtune: one process, two "
+                         "GPUs, launch-setting sweep of push and pull plus plain peer copies; store: "
+                         "store_kvcache only")
     ap.add_argument("--pull", action="store_true", help="pair1p: destination pulls instead of source pushing")
     ap.add_argument("--pair-mode", choices=["auto", "push", "pull"], default="auto",
                     help="N>1 exchanges that send both ways at once (phase A, config 5): auto = push")
@@ -1503,6 +1638,8 @@ def main() -> None:
         res = bench_config5(args)
     elif args.workload == "pair1p":
         res = bench_pair_one_process(args)
+    elif args.workload == "pairtune":
+        res = bench_pair_tuning(args)
     elif args.workload == "store":
         torch.cuda.set_device(0)
         res = bench_store_kvcache(0, hbm_peak()[0], iters=max(3, args.steps), num_blocks=args.cache_blocks)
