@@ -1412,6 +1412,74 @@ def bench_pair_one_process(args) -> dict:
             "GB/s": P / (ms * 1e-3) / 1e9, "frac_nvlink": P / (ms * 1e-3) / 1e9 / NVLINK_NOMINAL_GBS, "verified": ok}
 
 
+def bench_local_tuning(args) -> dict:
+    """``--workload localtune``: 1-GPU moves at config 2 geometry for B in
+    {1, 4, 16, 64} over a grid of launch settings (bulk ring stages x tile x
+    CTAs per SM, and the register engine), L2 flushed (written, then another
+    buffer read) before every timed launch, median of 20 launches; each
+    setting's result checked byte for byte. Measurement sweep behind the
+    automatic choice for small moves."""
+    import itertools
+
+    from lmpool_b200 import _capi
+    from lmpool_b200 import kv_transfer as kt
+    from lmpool_b200.layout import affine_layout
+
+    g = dict(LOCAL)
+    g["N"] = args.cache_blocks or 256
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cache = torch.empty((2, g["L"], g["N"], g["bs"], g["H"], g["D"]), dtype=torch.bfloat16, device=dev)
+    cache.normal_(generator=torch.Generator(device=dev).manual_seed(0))
+    lay = affine_layout(cache, g["L"])
+    perm = seeded_perm(g["N"], 0)
+    stream = torch.cuda.current_stream(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = L2Flush(dev)
+    peak, _ = hbm_peak()
+    lib = _capi.lib()
+    old = _capi.Tuning()
+    lib.kvx_get_tuning(_capi.ctypes.byref(old))
+    grid = [(0, 0, 0, 0)]
+    for stages, tile, cps in itertools.product([4, 6, 8], [8192, 16384, 32768], [0, 1, 2, 4]):
+        grid.append((2, cps, tile, stages))
+    grid += [(1, cps, tile, 0) for cps in (2, 4, 8) for tile in (16384, 32768)]
+    out = {}
+    try:
+        for b in (1, 4, 16, 64):
+            s_t = torch.tensor(perm[:b], dtype=torch.int64, device=dev)
+            d_t = torch.tensor(perm[b:2 * b], dtype=torch.int64, device=dev)
+            pb = payload_bytes(g, b)
+            rows = []
+            for variant, cps, tile, stages in grid:
+                _capi.check(lib.kvx_set_tuning(_capi.ctypes.byref(_capi.Tuning(variant, cps, tile, stages))),
+                            "kvx_set_tuning")
+                for _ in range(3):
+                    kt._launch_move(0, lay, lay, s_t, d_t, b, status, stream)
+                times = []
+                for _ in range(20):
+                    flush()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    kt._launch_move(0, lay, lay, s_t, d_t, b, status, stream)
+                    e1.record(stream)
+                    e1.synchronize()
+                    times.append(e0.elapsed_time(e1))
+                us = statistics.median(times) * 1e3
+                rows.append({"variant": {0: "auto", 1: "register", 2: "bulk"}[variant], "ctas_per_sm": cps,
+                             "tile": tile, "stages": stages, "us": us,
+                             "frac_hbm": 2 * pb / (us * 1e-6) / 1e9 / peak,
+                             "verified_bitexact": verify_local(cache, perm[:b], perm[b:2 * b])["chunks_mismatched"] == 0})
+            out[str(b)] = {"automatic": rows[0], "best": min(rows, key=lambda r: r["us"]), "rows": rows}
+    finally:
+        lib.kvx_set_tuning(_capi.ctypes.byref(old))
+    if int(status.item()):
+        raise RuntimeError(f"kernel status {int(status.item())}")
+    return {"workload": "local move tuning sweep, config 2 geometry, small B, L2 flushed before each launch",
+            "cache_blocks": g["N"], "results": out,
+            "verified_bitexact": all(r["verified_bitexact"] for v in out.values() for r in v["rows"])}
+
+
 def bench_pair_tuning(args) -> dict:
     """``--workload pairtune``: the pair transfer at Qwen3-8B geometry on
     cuda:0 and cuda:1 in one process, over a grid of launch settings (bulk
@@ -1606,10 +1674,12 @@ def main() -> None:
     ap.add_argument("--cache-blocks", type=int, default=0,
                     help="1-GPU cache size in blocks (default: config 2's 2048); for small profiling cases")
     ap.add_argument("--blocks", type=int, default=0, help="1-GPU blocks moved per step (default 512)")
-    ap.add_argument("--workload", choices=["default", "config5", "pair1p", "pairtune", "store"], default="default",
+    ap.add_argument("--workload", choices=["default", "config5", "pair1p", "pairtune", "localtune", "store"],
+                    default="default",
                     help="config5: benchmark config 5 transfer + store_kvcache overlap (N >= 2 GPUs); "
                          "pair1p: one process, two GPUs, pair push (profiling); pairtune: one process, two "
-                         "GPUs, launch-setting sweep of push and pull plus plain peer copies; store: "
+                         "GPUs, launch-setting sweep of push and pull plus plain peer copies; localtune: the same for "
+                         "small 1-GPU moves; store: "
                          "store_kvcache only")
     ap.add_argument("--pull", action="store_true", help="pair1p: destination pulls instead of source pushing")
     ap.add_argument("--pair-mode", choices=["auto", "push", "pull"], default="auto",
@@ -1640,6 +1710,8 @@ def main() -> None:
         res = bench_pair_one_process(args)
     elif args.workload == "pairtune":
         res = bench_pair_tuning(args)
+    elif args.workload == "localtune":
+        res = bench_local_tuning(args)
     elif args.workload == "store":
         torch.cuda.set_device(0)
         res = bench_store_kvcache(0, hbm_peak()[0], iters=max(3, args.steps), num_blocks=args.cache_blocks)
