@@ -223,7 +223,10 @@ int kvx_pair_push(int32_t device, const kvx_cache_desc* src, const kvx_mailbox* 
  *                        the launch completes.
  *   kvx_pair_wait_pulled (source, optional) waits (bounded) until the
  *                        destination reports a pull newer than the last one
- *                        consumed; FAIL -> KVX_DEV_PEER_FAILED.
+ *                        consumed and at least as new as the last token this
+ *                        rank granted it (a report of an earlier transfer the
+ *                        source did not wait for never satisfies a newer
+ *                        one); FAIL -> KVX_DEV_PEER_FAILED.
  * A push arm and a pull request never satisfy each other (the count words
  * differ), so two ends that disagree on the mode fail instead of moving data.
  * Measured on B200 at Qwen3-8B geometry, B=64: 777 GB/s per direction for
@@ -280,7 +283,7 @@ int kvx_mailbox_destroy(int32_t device, const kvx_mailbox* mailbox);
 /* Last completion token this rank received from `src_rank` (host read). */
 int kvx_mailbox_read_done(int32_t device, const kvx_mailbox* mailbox, int32_t src_rank, uint64_t* token_out);
 /* Zero every word of `peer`'s pair state in this rank's own mailbox (arm,
- * count, done, consumed, go, pulled and both CTA counters), enqueued on
+ * count, done, consumed, go, pulled, granted and both CTA counters), enqueued on
  * `stream`. Both ranks of a pair call it, with no transfer of that pair in
  * flight, before they start again from token 1: how a pair disabled after a
  * timeout is brought back without recreating the mailbox (prewarm does it). */

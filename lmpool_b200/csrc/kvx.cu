@@ -304,14 +304,15 @@ __global__ void __launch_bounds__(32) move_bulk_kernel(const __grid_constant__ M
 // ---------------------------------------------------------------------------
 
 struct MailboxLayout {
-    uint64_t arm, done, count, consumed, go, pulled, pull_consumed, counter, pull_counter, ids, total;
+    uint64_t arm, done, count, consumed, go, pulled, pull_consumed, granted, counter, pull_counter, ids, total;
 };
 
 // Per peer p: arm[p], count[p], ids[p][] (written by destination p, push),
 // done[p] (written by source p, push), consumed[p], go[p] (local, push),
 // pulled[p] (written by destination p after it pulled from this rank),
-// pull_consumed[p] (local), counter[p] / pull_counter[p] (CTA completion
-// counters of this rank's push to p / pull from p).
+// pull_consumed[p] (local), granted[p] (local: the last token this rank
+// granted to p), counter[p] / pull_counter[p] (CTA completion counters of
+// this rank's push to p / pull from p).
 __host__ __device__ inline MailboxLayout mailbox_layout(int64_t peers, int64_t max_blocks) {
     MailboxLayout m;
     m.arm = 0;
@@ -321,7 +322,8 @@ __host__ __device__ inline MailboxLayout mailbox_layout(int64_t peers, int64_t m
     m.go = m.consumed + 8 * peers;
     m.pulled = m.go + 8 * peers;
     m.pull_consumed = m.pulled + 8 * peers;
-    m.counter = m.pull_consumed + 8 * peers;
+    m.granted = m.pull_consumed + 8 * peers;
+    m.counter = m.granted + 8 * peers;
     m.pull_counter = m.counter + 4 * peers;
     m.ids = (m.pull_counter + 4 * peers + 255) / 256 * 256;
     m.total = m.ids + 8 * peers * max_blocks;
@@ -352,14 +354,15 @@ __global__ void __launch_bounds__(1024) publish_kernel(const int64_t* ids, int64
 // destination and check the posted count word.
 //   push (go != nullptr): record the token the push will signal in *go
 //     (0 = do not run); a count mismatch answers token | FAIL in remote_done.
-//   grant (go == nullptr): answer the token itself in remote_done. The store
+//   grant (go == nullptr): record the token in *granted and answer it in
+//     remote_done. The store
 //     is ordered after every earlier kernel of this stream (they completed
 //     before this one started, and the fence makes their writes visible to
 //     the system), so the destination reads the blocks only after the
 //     source's own writes to them.
 __global__ void wait_armed_kernel(const uint64_t* arm, const uint64_t* count, uint64_t* consumed, uint64_t* go,
-                                  uint64_t* remote_done, uint64_t expected_count, uint64_t timeout_ns,
-                                  int32_t* status) {
+                                  uint64_t* granted, uint64_t* remote_done, uint64_t expected_count,
+                                  uint64_t timeout_ns, int32_t* status) {
     if (threadIdx.x != 0) return;
     const uint64_t last = ld_relaxed_gpu(consumed);
     const uint64_t t0 = global_timer_ns();
@@ -378,6 +381,7 @@ __global__ void wait_armed_kernel(const uint64_t* arm, const uint64_t* count, ui
             } else if (go != nullptr) {
                 *go = v;
             } else {
+                if (granted != nullptr) *granted = v;
                 __threadfence_system();
                 st_release_sys(remote_done, v);
             }
@@ -410,15 +414,21 @@ __global__ void wait_done_kernel(const uint64_t* done, uint64_t token, uint64_t 
 }
 
 // Source (pull mode): wait until the destination reports a pull newer than
-// the last one consumed from it; FAIL bit -> the destination's pull failed.
-__global__ void wait_pulled_kernel(const uint64_t* pulled, uint64_t* consumed, uint64_t timeout_ns, int32_t* status) {
+// the last one consumed from it and at least as new as the last token this
+// rank granted it (so a report left over from an earlier transfer whose
+// source did not wait for it never satisfies a newer one); FAIL bit -> the
+// destination's pull failed.
+__global__ void wait_pulled_kernel(const uint64_t* pulled, uint64_t* consumed, const uint64_t* granted,
+                                   uint64_t timeout_ns, int32_t* status) {
     if (threadIdx.x != 0) return;
-    const uint64_t last = ld_relaxed_gpu(consumed);
+    const uint64_t last = ld_relaxed_gpu(consumed) & ~kFailBit;
+    const uint64_t want = ld_relaxed_gpu(granted);
     const uint64_t t0 = global_timer_ns();
     const uint64_t max_polls = timeout_ns / 64 + 1000000ull;
     for (uint64_t poll = 0; poll < max_polls; ++poll) {
         const uint64_t v = ld_acquire_sys(pulled);
-        if ((v & ~kFailBit) > (last & ~kFailBit)) {
+        const uint64_t token = v & ~kFailBit;
+        if (token > last && token >= want) {
             *consumed = v;
             __threadfence();
             if (v & kFailBit) atomicOr(status, KVX_DEV_PEER_FAILED);
@@ -1022,7 +1032,7 @@ int kvx_pair_wait_armed(int32_t device, const kvx_mailbox* my_mb, const kvx_mail
     const MailboxLayout md = mailbox_layout(dst_mb->max_peers, dst_mb->max_blocks);
     wait_armed_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
         mb_ptr<uint64_t>(my_mb, m.arm, dst_rank), mb_ptr<uint64_t>(my_mb, m.count, dst_rank),
-        mb_ptr<uint64_t>(my_mb, m.consumed, dst_rank), mb_ptr<uint64_t>(my_mb, m.go, dst_rank),
+        mb_ptr<uint64_t>(my_mb, m.consumed, dst_rank), mb_ptr<uint64_t>(my_mb, m.go, dst_rank), nullptr,
         mb_ptr<uint64_t>(dst_mb, md.done, my_rank), static_cast<uint64_t>(num_ids), timeout_ns, status_dev);
     KVX_CUDA(cudaGetLastError(), "launch wait-armed kernel");
     return KVX_OK;
@@ -1061,8 +1071,9 @@ int kvx_pair_grant(int32_t device, const kvx_mailbox* my_mb, const kvx_mailbox* 
     const MailboxLayout md = mailbox_layout(dst_mb->max_peers, dst_mb->max_blocks);
     wait_armed_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
         mb_ptr<uint64_t>(my_mb, m.arm, dst_rank), mb_ptr<uint64_t>(my_mb, m.count, dst_rank),
-        mb_ptr<uint64_t>(my_mb, m.consumed, dst_rank), nullptr, mb_ptr<uint64_t>(dst_mb, md.done, my_rank),
-        static_cast<uint64_t>(num_ids) | kPullTag, timeout_ns, status_dev);
+        mb_ptr<uint64_t>(my_mb, m.consumed, dst_rank), nullptr, mb_ptr<uint64_t>(my_mb, m.granted, dst_rank),
+        mb_ptr<uint64_t>(dst_mb, md.done, my_rank), static_cast<uint64_t>(num_ids) | kPullTag, timeout_ns,
+        status_dev);
     KVX_CUDA(cudaGetLastError(), "launch grant kernel");
     return KVX_OK;
 }
@@ -1074,7 +1085,7 @@ int kvx_mailbox_reset_peer(int32_t device, const kvx_mailbox* mailbox, int32_t p
     KVX_DEVICE_GUARD(device);
     const MailboxLayout m = mailbox_layout(mailbox->max_peers, mailbox->max_blocks);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const uint64_t words[] = {m.arm, m.done, m.count, m.consumed, m.go, m.pulled, m.pull_consumed};
+    const uint64_t words[] = {m.arm, m.done, m.count, m.consumed, m.go, m.pulled, m.pull_consumed, m.granted};
     for (uint64_t off : words)
         KVX_CUDA(cudaMemsetAsync(mb_ptr<uint64_t>(mailbox, off, peer), 0, sizeof(uint64_t), st), "reset mailbox");
     KVX_CUDA(cudaMemsetAsync(mb_ptr<unsigned int>(mailbox, m.counter, peer), 0, sizeof(unsigned int), st),
@@ -1385,8 +1396,8 @@ int kvx_pair_wait_pulled(int32_t device, const kvx_mailbox* my_mb, int32_t dst_r
     KVX_DEVICE_GUARD(device);
     const MailboxLayout m = mailbox_layout(my_mb->max_peers, my_mb->max_blocks);
     wait_pulled_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        mb_ptr<uint64_t>(my_mb, m.pulled, dst_rank), mb_ptr<uint64_t>(my_mb, m.pull_consumed, dst_rank), timeout_ns,
-        status_dev);
+        mb_ptr<uint64_t>(my_mb, m.pulled, dst_rank), mb_ptr<uint64_t>(my_mb, m.pull_consumed, dst_rank),
+        mb_ptr<uint64_t>(my_mb, m.granted, dst_rank), timeout_ns, status_dev);
     KVX_CUDA(cudaGetLastError(), "launch wait-pulled kernel");
     return KVX_OK;
 }

@@ -820,3 +820,32 @@ def test_a_deferred_grant_is_read_later_and_a_failed_one_disables_the_pair(requi
         ep0.get_link(1)
     ep0.close()
     ep1.close()
+
+
+def test_a_report_left_by_an_earlier_transfer_does_not_satisfy_a_newer_wait(require_gpu):
+    """A source that returned once granted leaves its transfer's pull report
+    unconsumed. A later transfer's wait for the destination's read must wait
+    for that transfer's own report, not take the old one."""
+    shape = (2, 3, 12, 16, 2, 32)
+    src_cpu, dst_cpu, src, dst, ep0, ep1, link01, link10 = _pair(0, 0, shape, 34)
+    s = torch.cuda.current_stream(0)
+    ids = kvgen.seeded_perm(12, 35)[:3]
+    ep0.status.zero_()
+    ep1.status.zero_()
+    _pull_steps(ep1, link10, ep0, link01, _ids(ids, 0), _ids(ids, 0), 3, s, s, wait_pulled=False)   # report left behind
+    token = ep1.next_token(0)
+    ep1.request(link10, 3, token, s)
+    ep0.grant(link01, 3, 5.0, s)
+    ep0.wait_pulled(1, 0.2, s)                       # the new transfer has not been read yet
+    with pytest.raises(_capi.KvxError, match="timed out"):
+        ep0.check_status(s, "source")
+    ep0.status.zero_()
+    ep1.wait_done(0, token, 5.0, s)
+    ep1.pull(ep1.cache, [(link10, link10.cache, _ids(ids, 0), _ids(ids, 0), 3, token)], s)
+    ep0.wait_pulled(1, 5.0, s)                       # now its own report is there
+    ep0.check_status(s, "source")
+    ep1.check_status(s, "destination")
+    c_oracle.swap_planned(src_cpu, ids, dst_cpu, ids, nthreads=2)
+    assert _same_bits(dst, dst_cpu)
+    ep0.close()
+    ep1.close()
