@@ -1225,13 +1225,26 @@ def bench_pairs(args) -> dict | None:
         step(other)
     other_ms = timed_max(dist, dev, stream, lambda: step(other), 10)
 
-    copies = peer_copy(ep, partner, rank, stream, dist)
+    # Legs beside the headline run under a guard: an exception that every
+    # rank meets at the same point is recorded in the line instead of losing
+    # it; a byte mismatch is not an exception and still fails the run.
+    errors: dict = {}
+
+    def guarded(name, fn):
+        try:
+            return fn()
+        except Exception as exc:  # noqa: BLE001 - recorded in the line
+            errors[name] = f"{type(exc).__name__}: {exc}"[:400]
+            return None
+
+    copies = guarded("peer_copy", lambda: peer_copy(ep, partner, rank, stream, dist))
     sweep = None
     if world == 2:   # one direction at a time: both modes, pull is the default of swap_in
-        sweep = pair_sweep(ep, cache, g, rank, stream, dist, "pull") + \
-            pair_sweep(ep, cache, g, rank, stream, dist, "push")
-        ok &= all(r["verified_bitexact"] for r in sweep)
-    ref_pair = reference_gpu_pair(cache, g, rank, dist) if world == 2 else None
+        sweep = guarded("pair_sweep", lambda: pair_sweep(ep, cache, g, rank, stream, dist, "pull") +
+                        pair_sweep(ep, cache, g, rank, stream, dist, "push"))
+        ok &= all(r["verified_bitexact"] for r in sweep or [])
+    ref_pair = guarded("reference_gpu_pair", lambda: reference_gpu_pair(cache, g, rank, dist)) if world == 2 \
+        else None
     if ref_pair is not None and sweep is not None:
         for row in [ref_pair] + ref_pair["sweep"]:
             mine = [r["ms"] for r in sweep if r["blocks"] == row["blocks"] and r["ids"] == "scattered"]
@@ -1243,37 +1256,49 @@ def bench_pairs(args) -> dict | None:
         for sched in ("concurrent", "rotated"):
             for m in ("push", "pull"):
                 key = m if sched == "concurrent" else f"{m}_{sched}"
-                phase_b[key] = all_partner(ep, cache, g, rank, world, stream, dist, m, sched)
-        ok &= all(v["ok"] for v in phase_b.values())
-        phase_b["reference_nccl"] = reference_all_partner(cache, g, rank, world, dist)
+                res = guarded(f"phase_b_{key}", lambda: all_partner(ep, cache, g, rank, world, stream, dist, m,
+                                                                     sched))
+                if res is not None:
+                    phase_b[key] = res
+                    ok &= res["ok"]
+        ref_b = guarded("phase_b_reference", lambda: reference_all_partner(cache, g, rank, world, dist))
+        if ref_b is not None:
+            phase_b["reference_nccl"] = ref_b
 
     # the reference's algorithm on the same GPUs for the headline workload
-    ref_a = reference_phase_a(cache, g, rank, world, dist, src_ids, partner_src, dst_ids)
-    ref_a["this_kernel_speedup"] = ref_a["ms_per_step"] / ms
+    ref_a = guarded("reference_phase_a", lambda: reference_phase_a(cache, g, rank, world, dist, src_ids, partner_src,
+                                                                    dst_ids))
+    if ref_a is not None:
+        ref_a["this_kernel_speedup"] = ref_a["ms_per_step"] / ms
 
     # end to end through swap_in (the API LMPool calls), then through swap_batch;
     # the destination blocks are zeroed before each and verified after it
     e2e_steps = max(3, min(args.steps, 20))
     scrub(cache, dst_ids)
-    e2e_in = e2e_swap_in(kt, cache, g, rank, partner, src_ids, partner_src, dst_ids, stream, dist, e2e_steps)
-    e2e_in_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist)
-    ok &= e2e_in_chk["chunks_mismatched"] == 0
+    e2e_in = guarded("e2e_swap_in", lambda: e2e_swap_in(kt, cache, g, rank, partner, src_ids, partner_src, dst_ids,
+                                                         stream, dist, e2e_steps))
+    e2e_in_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist) if e2e_in else None
+    ok &= e2e_in_chk is None or e2e_in_chk["chunks_mismatched"] == 0
     scrub(cache, dst_ids)
-    for _ in range(2):
-        kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode)
-    batch_ms = timed_max(dist, dev, stream,
+
+    def batch_leg():
+        for _ in range(2):
+            kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode)
+        return timed_max(dist, dev, stream,
                          lambda: kt.swap_batch([(partner, src_ids)], [(partner, partner_src, dst_ids)], mode=mode),
                          e2e_steps)
-    e2e_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist)
-    ok &= e2e_chk["chunks_mismatched"] == 0
+
+    batch_ms = guarded("e2e_swap_batch", batch_leg)
+    e2e_chk = verify_moves(cache, {partner: src_ids}, {partner: dst_ids}, dist) if batch_ms else None
+    ok &= e2e_chk is None or e2e_chk["chunks_mismatched"] == 0
     kt.shutdown()
     kt._REGISTERED.pop(local, None)
     del cache
     ep = None
     torch.cuda.empty_cache()
 
-    c5 = config5_leg(kt, rank, world, dist, args.steps, mode)
-    ok &= c5["verified_bitexact"]
+    c5 = guarded("config5", lambda: config5_leg(kt, rank, world, dist, args.steps, mode))
+    ok &= c5 is None or c5["verified_bitexact"]
     oks = [None] * world
     dist.all_gather_object(oks, bool(ok))
     dist.barrier()
@@ -1282,7 +1307,22 @@ def bench_pairs(args) -> dict | None:
         return None
     if not all(oks):
         raise RuntimeError("pair transfer verification failed")
-    cpu = cpu_baseline_gloo(g, CPU_SAMPLE_BLOCKS, both_ways=True, seconds=10.0)
+    cpu = guarded("cpu_baseline", lambda: cpu_baseline_gloo(g, CPU_SAMPLE_BLOCKS, both_ways=True, seconds=10.0))
+    if e2e_in is not None:
+        e2e = {"value": world * P / (e2e_in["ms_per_step"] * 1e-3) / 1e9, "unit": "GB/s",
+               "ms_per_step": e2e_in["ms_per_step"], "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 8,
+               "api": "lmpool_b200.kv_transfer.swap_in(negotiate_blocks=False), host id lists: per pair 0->1 then "
+                      "1->0 as two plans (LMPool runs one plan per pair at a time), pull mode",
+               "source_call_ms": e2e_in["source_call_ms"]}
+    elif batch_ms:
+        e2e = {"value": world * P / (batch_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": batch_ms,
+               "h2d_bytes_per_step": 3 * B * 8, "d2h_bytes_per_step": 4,
+               "api": f"lmpool_b200.kv_transfer.swap_batch (both directions at once, {mode})"}
+    else:
+        e2e = None
+    if e2e is not None and batch_ms:
+        e2e["swap_batch"] = {"value": world * P / (batch_ms * 1e-3) / 1e9, "ms_per_step": batch_ms,
+                             "api": f"lmpool_b200.kv_transfer.swap_batch (both directions at once, {mode})"}
     value = world * P / (ms * 1e-3) / 1e9
     per_dir = P / (ms * 1e-3) / 1e9
     wire_per_block = profile_value("push_nvlink_pair", "nvlink_tx_bytes_per_block")
@@ -1303,15 +1343,9 @@ def bench_pairs(args) -> dict | None:
                      "peer_copy_measured": copies,
                      "frac_of_measured_peer_copy": (per_dir / copies["both_directions_GB/s_per_direction"])
                      if copies else None},
-        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
-        "cpu_baseline_host": cpu["host"],
-        "e2e": {"value": world * P / (e2e_in["ms_per_step"] * 1e-3) / 1e9, "unit": "GB/s",
-                "ms_per_step": e2e_in["ms_per_step"], "h2d_bytes_per_step": 2 * B * 8, "d2h_bytes_per_step": 8,
-                "api": "lmpool_b200.kv_transfer.swap_in(negotiate_blocks=False), host id lists: per pair 0->1 then "
-                       "1->0 as two plans (LMPool runs one plan per pair at a time), pull mode",
-                "source_call_ms": e2e_in["source_call_ms"],
-                "swap_batch": {"value": world * P / (batch_ms * 1e-3) / 1e9, "ms_per_step": batch_ms,
-                               "api": f"lmpool_b200.kv_transfer.swap_batch (both directions at once, {mode})"}},
+        "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")} if cpu else None,
+        "cpu_baseline_host": cpu["host"] if cpu else None,
+        "e2e": e2e,
         "gpu_launches": (4 if mode == "push" else 5) * args.steps,
         "transfer_mode": mode,
         "verified_bitexact": True,
@@ -1331,6 +1365,7 @@ def bench_pairs(args) -> dict | None:
         "reference_gpu_path": ref_pair,
         "phase_b": ({m: {k: v for k, v in r.items() if k != "ok"} for m, r in phase_b.items()} if phase_b else None),
         "config5": c5,
+        "errors": errors or None,
     }
 
 
