@@ -896,10 +896,10 @@ def all_partner(ep, cache, g: dict, rank: int, world: int, stream, dist, mode: s
     every other rank, into disjoint reserved sets.
 
     ``concurrent``: one exchange per step carries every destination and
-    source at once (one push or pull launch per rank). ``rotated``: world-1
-    exchanges per step; in exchange j rank r sends to r+j and receives from
-    r-j, so at any moment every GPU has one sender and one receiver, the
-    traffic pattern of disjoint pairs."""
+    source at once (one push or pull launch per rank). ``rotated``: one
+    exchange per round of a round-robin tournament over the ranks; in each
+    round every GPU exchanges both ways with one partner, the traffic
+    pattern of disjoint pairs."""
     dev = torch.device("cuda", ep.device)
     N, B = g["N"], PHASE_B_BLOCKS
     peers = [r for r in range(world) if r != rank]

@@ -106,6 +106,21 @@ class PeerLink:
     poisoned: str | None = None
 
 
+def pair_round(a: int, b: int, world_size: int) -> int:
+    """Round of the pair {a, b} in a round-robin tournament over
+    ``world_size`` ranks (the circle method): rank m-1 (m = world_size
+    rounded up to even) meets rank r in round r; any other two ranks meet in
+    the round r with a + b = 2r (mod m-1). Each of the m-1 rounds is a
+    perfect matching, and the value is the same for (a, b) and (b, a)."""
+    a, b = int(a), int(b)
+    if a == b or not (0 <= a < world_size and 0 <= b < world_size):
+        raise RuntimeError(f"no round for the pair ({a}, {b}) among {world_size} ranks")
+    m = world_size + (world_size % 2)
+    if a == m - 1 or b == m - 1:
+        return b if a == m - 1 else a
+    return ((a + b) * (m // 2)) % (m - 1)
+
+
 class TransferEndpoint:
     """Mailbox, peer links and pair tokens of one rank on one GPU."""
 
@@ -474,24 +489,27 @@ class TransferEndpoint:
     def exchange_rotated(self, mode: str, local: CacheLayout, outgoing: list[tuple], incoming: list[tuple],
                          timeout_s: float | None, stream, peer_layouts: dict | None = None,
                          wait_pulled: bool = True) -> None:
-        """The transfers of ``exchange`` in world_size-1 rounds.
+        """The transfers of ``exchange`` in rounds of disjoint pairs.
 
-        A transfer a->b belongs to round (b - a) mod world_size on both of its
-        ranks, so in round j this rank sends to rank+j and receives from
-        rank-j: every GPU has at most one sender and one receiver at a time
-        (the traffic of disjoint pairs) instead of all peers at once. Each
-        rank enqueues its rounds in increasing order and a round only waits
-        on that round's steps of its two peers, so no wait depends on a later
-        round. Every rank of a call must use this schedule.
+        Rounds follow a round-robin tournament over the ranks
+        (:func:`pair_round`): each round pairs every rank with at most one
+        partner, and both directions between two ranks fall in the same
+        round. So at any moment every GPU sends to one peer and receives from
+        that peer (the traffic of disjoint pairs exchanging both ways)
+        instead of serving all peers at once, and a pair that sends both ways
+        is never split across rounds. Each rank enqueues its rounds in
+        increasing order and a round only waits on that round's steps of its
+        one partner, so no wait depends on a later round. Every rank of a call
+        must use this schedule.
         """
         if mode not in ("push", "pull"):
             raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull' or 'push'")
         world = self.world_size
         rounds: dict[int, tuple[list, list]] = {}
         for item in outgoing:
-            rounds.setdefault((item[0] - self.rank) % world, ([], []))[0].append(item)
+            rounds.setdefault(pair_round(self.rank, item[0], world), ([], []))[0].append(item)
         for item in incoming:
-            rounds.setdefault((self.rank - item[0]) % world, ([], []))[1].append(item)
+            rounds.setdefault(pair_round(item[0], self.rank, world), ([], []))[1].append(item)
         for j in sorted(rounds):
             out, inc = rounds[j]
             self.exchange(mode, local, out, inc, timeout_s, stream, peer_layouts, wait_pulled)

@@ -790,11 +790,12 @@ def swap_batch(outgoing: list[tuple[int, List[int]]], incoming: list[tuple[int, 
     transfer must use the same one. Measured on B200: pull is ~10% faster for
     one-way traffic, push ~7% faster when a pair sends both ways at once.
     ``schedule`` orders transfers with several peers: ``"rotated"`` runs
-    them in world_size-1 rounds, round j sending to rank+j and receiving
-    from rank-j (measured on 4 B200s, all-partner exchange: 688 vs 648 GB/s
-    per GPU pushed, 640 vs 585 pulled); ``"concurrent"`` puts every peer in
-    one launch, which saves the per-round handshakes when transfers are
-    small. Every rank of the call must pass the same schedule.
+    them in the rounds of a round-robin tournament over the ranks (each
+    round a set of disjoint pairs, both directions of a pair in the same
+    round; all-partner exchange on 4 B200s, push: 688 vs 648 GB/s per GPU
+    with every peer at once); ``"concurrent"`` puts every peer in one
+    launch, which saves the per-round handshakes when transfers are small.
+    Every rank of the call must pass the same schedule.
     """
     if schedule not in ("rotated", "concurrent"):
         raise RuntimeError(f"unknown schedule {schedule!r}: expected 'rotated' or 'concurrent'")

@@ -104,21 +104,48 @@ def test_registered_cache_check_accepts_views_and_the_tensor_and_refuses_others(
         kt._check_registered(ep, t, 4)
 
 
-def test_rotated_schedule_puts_each_transfer_in_round_peer_offset():
+def test_rotated_schedule_runs_one_tournament_round_per_partner():
+    """Rounds are a round-robin tournament: both directions of a pair share
+    a round, each round gives every rank one partner."""
+    from lmpool_b200.endpoint import pair_round
+
+    for n in range(2, 10):
+        rounds: dict = {}
+        for a in range(n):
+            for b in range(a + 1, n):
+                r = pair_round(a, b, n)
+                assert r == pair_round(b, a, n)
+                rounds.setdefault(r, []).append((a, b))
+        assert sorted(rounds) == list(range(n - 1 + n % 2))
+        for pairs in rounds.values():
+            members = [x for pair in pairs for x in pair]
+            assert len(members) == len(set(members))
+    with pytest.raises(RuntimeError, match="no round"):
+        pair_round(1, 1, 4)
     ep, calls = _endpoint(1, 4)
     ep.exchange_rotated("push", "local", [(2, "i2", 5), (0, "i0", 6)], [(3, "s3", "d3", 7), (0, "s0", "d0", 8)],
                         1.0, None)
-    # round j sends to rank+j and receives from rank-j (mod 4): j=1 out 2 and in 0, j=2 in 3, j=3 out 0
-    pushes = [c[1] for c in calls if c[0] == "push"]
-    publishes = [(c[1], c[2]) for c in calls if c[0] == "publish"]
-    assert pushes == [[(2, "cache2", 5)], [(0, "cache0", 6)]]
-    assert publishes == [(0, 8), (3, 7)]
+    # 4 ranks: {1,3} meet in round 1, {1,2} in round 0, {0,1} in round 2: the pair with
+    # rank 0 sends and receives in the same round
     kinds = [c[0] for c in calls]
-    assert kinds == ["publish", "wait_armed", "push", "wait_done",   # round 1
-                     "publish", "wait_done",                         # round 2
-                     "wait_armed", "push"]                           # round 3
+    assert kinds == ["wait_armed", "push",                             # round 0: to 2
+                     "publish", "wait_done",                           # round 1: from 3
+                     "publish", "wait_armed", "push", "wait_done"]     # round 2: both ways with 0
+    assert [c[1] for c in calls if c[0] == "push"] == [[(2, "cache2", 5)], [(0, "cache0", 6)]]
+    assert [(c[1], c[2]) for c in calls if c[0] == "publish"] == [(3, 7), (0, 8)]
     with pytest.raises(RuntimeError, match="mode"):
         ep.exchange_rotated("sideways", "local", [], [], 1.0, None)
+
+
+def test_disjoint_pairs_exchange_both_ways_in_a_single_round():
+    """Phase A through the rotated schedule at 4 and 8 ranks: every pair
+    sends both ways in one round (one exchange call per rank)."""
+    for world in (4, 8):
+        for r in range(world):
+            ep, calls = _endpoint(r, world)
+            partner = r + 1 if r % 2 == 0 else r - 1
+            ep.exchange_rotated("push", "local", [(partner, "i", 3)], [(partner, "s", "d", 3)], 1.0, None)
+            assert [c[0] for c in calls] == ["publish", "wait_armed", "push", "wait_done"]
 
 
 def _simulate(streams: dict[int, list], mode: str) -> None:
