@@ -501,9 +501,15 @@ class TransferEndpoint:
         increasing order and a round only waits on that round's steps of its
         one partner, so no wait depends on a later round. Every rank of a call
         must use this schedule.
+
+        ``mode="auto"`` picks the mode per round: push when this rank and its
+        partner send each other blocks in that round (writes cost fewer wire
+        bytes than reads when both directions are busy), pull when the round
+        is one-way (reads cost fewer). Both ranks of a round see the same
+        pair of lists, so they pick the same mode.
         """
-        if mode not in ("push", "pull"):
-            raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull' or 'push'")
+        if mode not in ("push", "pull", "auto"):
+            raise RuntimeError(f"unknown transfer mode {mode!r}: expected 'pull', 'push' or 'auto'")
         world = self.world_size
         rounds: dict[int, tuple[list, list]] = {}
         for item in outgoing:
@@ -512,7 +518,11 @@ class TransferEndpoint:
             rounds.setdefault(pair_round(item[0], self.rank, world), ([], []))[1].append(item)
         for j in sorted(rounds):
             out, inc = rounds[j]
-            self.exchange(mode, local, out, inc, timeout_s, stream, peer_layouts, wait_pulled)
+            round_mode = mode
+            if mode == "auto":
+                two_way = {o[0] for o in out} & {i[0] for i in inc}
+                round_mode = "push" if two_way else "pull"
+            self.exchange(round_mode, local, out, inc, timeout_s, stream, peer_layouts, wait_pulled)
 
     def read_done(self, src_rank: int) -> int:
         out = ctypes.c_uint64(0)

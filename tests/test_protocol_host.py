@@ -195,9 +195,9 @@ def _simulate(streams: dict[int, list], mode: str) -> None:
     assert not arm and not done and not any(pulled.values())
 
 
-@pytest.mark.parametrize("mode", ["push", "pull"])
-@pytest.mark.parametrize("schedule", ["concurrent", "rotated"])
-@pytest.mark.parametrize("world,seed", [(2, 0), (4, 1), (6, 2), (8, 3), (8, 4)])
+@pytest.mark.parametrize("mode,schedule", [("push", "concurrent"), ("pull", "concurrent"), ("push", "rotated"),
+                                           ("pull", "rotated"), ("auto", "rotated")])
+@pytest.mark.parametrize("world,seed", [(2, 0), (4, 1), (5, 5), (6, 2), (8, 3), (8, 4)])
 def test_every_rank_finishes_for_random_transfer_sets(mode, schedule, world, seed):
     """Any set of directed transfers, each rank calling the same schedule
     several times in a row, completes without a deadlock."""
@@ -356,3 +356,23 @@ def test_source_return_setting_picks_the_source_side_path(monkeypatch):
     ep.mode = "pull"
     with pytest.raises(RuntimeError, match="LMPOOL_B200_SOURCE_RETURN"):
         kt._source_side(ep, 1, [7], 1.0, None)
+
+
+def test_auto_mode_pushes_two_way_rounds_and_pulls_one_way_rounds():
+    ep, calls = _endpoint(1, 4)
+    # partner 0 both ways (round 2), partner 2 one way out (round 0), partner 3 one way in (round 1)
+    ep.exchange_rotated("auto", "local", [(0, "i0", 2), (2, "i2", 3)], [(0, "s0", "d0", 2), (3, "s3", "d3", 4)],
+                        1.0, None)
+    kinds = [c[0] for c in calls]
+    assert kinds == ["grant", "wait_pulled",                                  # round 0: pull, to 2
+                     "request", "wait_done", "pull",                          # round 1: pull, from 3
+                     "publish", "wait_armed", "push", "wait_done"]           # round 2: push, both ways with 0
+
+
+def test_swap_batch_refuses_auto_without_rounds(monkeypatch):
+    kt, calls = _batch_setup(monkeypatch)
+    with pytest.raises(RuntimeError, match="needs schedule='rotated'"):
+        kt.swap_batch([(1, [0])], [], mode="auto", schedule="concurrent")
+    with pytest.raises(RuntimeError, match="unknown transfer mode"):
+        kt.swap_batch([(1, [0])], [], mode="sideways")
+    assert calls == []
