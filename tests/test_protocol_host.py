@@ -125,12 +125,12 @@ def test_rotated_schedule_runs_one_tournament_round_per_partner():
     ep, calls = _endpoint(1, 4)
     ep.exchange_rotated("push", "local", [(2, "i2", 5), (0, "i0", 6)], [(3, "s3", "d3", 7), (0, "s0", "d0", 8)],
                         1.0, None)
-    # 4 ranks: {1,3} meet in round 1, {1,2} in round 0, {0,1} in round 2: the pair with
+    # 4 ranks: {1,3} meet in schedule step 1, {1,2} in step 0, {0,1} in step 2: the pair with
     # rank 0 sends and receives in the same round
     kinds = [c[0] for c in calls]
-    assert kinds == ["wait_armed", "push",                             # round 0: to 2
-                     "publish", "wait_done",                           # round 1: from 3
-                     "publish", "wait_armed", "push", "wait_done"]     # round 2: both ways with 0
+    assert kinds == ["wait_armed", "push",                             # step 0: to 2
+                     "publish", "wait_done",                           # step 1: from 3
+                     "publish", "wait_armed", "push", "wait_done"]     # step 2: both ways with 0
     assert [c[1] for c in calls if c[0] == "push"] == [[(2, "cache2", 5)], [(0, "cache0", 6)]]
     assert [(c[1], c[2]) for c in calls if c[0] == "publish"] == [(3, 7), (0, 8)]
     with pytest.raises(RuntimeError, match="mode"):
@@ -360,13 +360,13 @@ def test_source_return_setting_picks_the_source_side_path(monkeypatch):
 
 def test_auto_mode_pushes_two_way_rounds_and_pulls_one_way_rounds():
     ep, calls = _endpoint(1, 4)
-    # partner 0 both ways (round 2), partner 2 one way out (round 0), partner 3 one way in (round 1)
+    # partner 0 both ways (step 2), partner 2 one way out (step 0), partner 3 one way in (step 1)
     ep.exchange_rotated("auto", "local", [(0, "i0", 2), (2, "i2", 3)], [(0, "s0", "d0", 2), (3, "s3", "d3", 4)],
                         1.0, None)
     kinds = [c[0] for c in calls]
-    assert kinds == ["grant", "wait_pulled",                                  # round 0: pull, to 2
-                     "request", "wait_done", "pull",                          # round 1: pull, from 3
-                     "publish", "wait_armed", "push", "wait_done"]           # round 2: push, both ways with 0
+    assert kinds == ["grant", "wait_pulled",                                  # step 0: pull, to 2
+                     "request", "wait_done", "pull",                          # step 1: pull, from 3
+                     "publish", "wait_armed", "push", "wait_done"]           # step 2: push, both ways with 0
 
 
 def test_swap_batch_refuses_auto_without_rounds(monkeypatch):
