@@ -9,10 +9,14 @@ sm_100a kernels of ``_kvx.so`` instead of ``index_select`` / NCCL
   per-layer helpers) are one kernel launch each over all layers, K/V planes
   and blocks.
 * ``swap_in(..., negotiate_blocks=False)`` -- the planned path the data plane
-  uses (model_runner.py:747-806) -- has no staging payload and no NCCL call:
-  the source reads its blocks from HBM and stores them straight into the
-  destination's reserved blocks over NVLink (CUDA IPC mapping), then
-  release-stores a completion token the destination waits for (bounded).
+  uses (model_runner.py:747-806) -- has no staging payload and no NCCL call.
+  Pull (default): the destination asks, the source grants from its own
+  stream once its earlier work there is done, and the destination's kernel
+  reads the source's blocks over NVLink (CUDA IPC mapping) straight into its
+  reserved blocks, then reports to the source. Push: the source's kernel
+  stores its blocks into the destination's reserved blocks and
+  release-stores a completion token the destination waits for. Every wait
+  is bounded.
 * ``prewarm_p2p_pairs`` maps every peer's KV cache and mailbox once (IPC
   handles exchanged with one ``all_gather_object`` on the world group, all
   ranks in the same order as the reference's group creation) and times one
