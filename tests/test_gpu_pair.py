@@ -346,7 +346,9 @@ def _fake_runner(rank: int, cache: torch.Tensor):
 
 def _api_worker(rank: int, port: int, queue, mode: str = "pull") -> None:
     """Rest of the drop-in surface across two processes: ModelRunner mixin,
-    negotiated swap_in, legacy swap_out, swap_batch both ways at once."""
+    negotiated swap_in, legacy swap_out, swap_batch both ways at once (in the
+    process's mode, then with mode="auto": a push round both ways, a pull
+    round one way)."""
     os.environ["LMPOOL_B200_KV_MODE"] = mode
     import torch.distributed as dist
 
@@ -416,6 +418,25 @@ def _api_worker(rank: int, port: int, queue, mode: str = "pull") -> None:
         c_oracle.swap_planned(model[1], out1, new0, in0, nthreads=4)
         model[0], model[1] = new0, new1
         check("swap_batch")
+        # 5. mode="auto": both ways at once (a push round), then one way (a pull round)
+        perm = kvgen.seeded_perm(40, 550)
+        out0, out1, in1, in0 = perm[:5], perm[5:10], perm[20:25], perm[25:30]
+        if rank == 0:
+            kt.swap_batch([(1, out0)], [(1, out1, in0)], timeout_s=20, mode="auto")
+        else:
+            kt.swap_batch([(0, out1)], [(0, out0, in1)], timeout_s=20, mode="auto")
+        new0, new1 = model[0].clone(), model[1].clone()
+        c_oracle.swap_planned(model[0], out0, new1, in1, nthreads=4)
+        c_oracle.swap_planned(model[1], out1, new0, in0, nthreads=4)
+        model[0], model[1] = new0, new1
+        check("swap_batch auto, both ways")
+        src, dst = perm[30:34], perm[34:38]
+        if rank == 0:
+            kt.swap_batch([(1, src)], [], timeout_s=20, mode="auto")
+        else:
+            kt.swap_batch([], [(0, src, dst)], timeout_s=20, mode="auto")
+        c_oracle.swap_planned(model[0], src, model[1], dst, nthreads=4)
+        check("swap_batch auto, one way")
         kt.shutdown()
         queue.put({"rank": rank, "errors": errors})
         dist.destroy_process_group()
